@@ -1,0 +1,87 @@
+"""ctypes binding of the C-ABI library `_morj_b200.so` (declared in `include/morj_b200.h`).
+
+The engine's only route to the GPU kernels. There is no fallback: if the library is missing or fails to load,
+`lib()` raises, and every wrapper raises on a non-zero status (`ValueError` for bad arguments, `MemoryError` for
+out-of-memory, `NativeFailure` otherwise), mirroring the reference engine's error classes.
+"""
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, '_morj_b200.so')
+
+OK, ERR_ARG, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
+EPI_STORE, EPI_GEGLU = 0, 1
+
+_lock = threading.Lock()
+_lib = None
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+LL = ctypes.c_longlong
+F = ctypes.c_float
+IP = ctypes.POINTER(ctypes.c_int)
+
+# name -> argument types (all return int, except morj_last_error)
+SIGNATURES = {
+    'morj_version': [],
+    'morj_device_error': [IP, I, P],
+    'morj_gemm_bf16': [P, LL, P, LL, P, LL, I, I, I, I, P],
+    'morj_embed_rmsnorm': [P, P, P, P, I, I, F, P, F, P, P, P],
+    'morj_qkv_post': [P, LL, I, I, I, I, I, P, P, P, P, P, F, P, P, P, P],
+    'morj_tree_attention_work': [IP, I, I, I, IP, I],
+    'morj_tree_attention': [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, F, P, I, P],
+    'morj_attn_epilogue': [P, P, P, P, P, I, I, F, P],
+    'morj_mlp_epilogue': [P, P, P, P, P, P, I, I, F, I, P],
+    'morj_gather_rows': [P, LL, P, I, I, P, LL, P],
+    'morj_scatter_rows': [P, LL, P, I, I, P, LL, P],
+    'morj_label_head': [P, LL, P, P, P, I, P, P, I, F, F, P, P],
+    'morj_geglu': [P, I, I, P, P],
+}
+
+
+class NativeFailure(RuntimeError):
+    """A native call failed for a reason other than bad arguments or memory (the engine treats it as fatal)."""
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(f'native library {LIB_PATH} is not built (python -m morj_b200.build)')
+                L = ctypes.CDLL(LIB_PATH)
+                for name, args in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.argtypes = args
+                    fn.restype = ctypes.c_int
+                L.morj_last_error.argtypes = []
+                L.morj_last_error.restype = ctypes.c_char_p
+                _lib = L
+    return _lib
+
+
+def check(status, what):
+    if status == OK:
+        return
+    msg = lib().morj_last_error().decode(errors='replace')
+    text = f'{what}: {msg}'
+    if status == ERR_ARG:
+        raise ValueError(text)
+    if status == ERR_OOM:
+        raise MemoryError(text)
+    raise NativeFailure(f'{text} (status {status})')
+
+
+def call(name, *args):
+    """Call entry point `name` and raise on a non-zero status."""
+    check(getattr(lib(), name)(*args), name)
+
+
+def device_error(stream, clear=True):
+    """The device error word (0 = no kernel reported a failure); synchronises `stream`."""
+    code = ctypes.c_int(0)
+    check(lib().morj_device_error(ctypes.byref(code), int(clear), stream), 'morj_device_error')
+    return code.value

@@ -1,0 +1,223 @@
+// Shared device helpers for the sm_100a kernels: mbarriers with bounded waits, TMA tile loads, tcgen05 (TMEM
+// allocation, UMMA issue/commit, TMEM loads), shared-memory matrix descriptors, BF16 packing, and the library's
+// error reporting. Every wait in this library is bounded: when a wait runs out, the kernel records the site in
+// the device error word, raises its CTA's abort flag, and returns through its normal exit path (TMEM freed).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "morj_b200.h"
+
+#define MORJ_DEV __device__ __forceinline__
+
+namespace morj {
+
+// ---------------------------------------------------------------------------------------------------------------
+// Error word shared by all kernels of the library (one per device): 0 = clean; otherwise the first failure's code.
+// Defined in rowops.cu; the library is built with relocatable device code so every kernel sees the same word.
+// ---------------------------------------------------------------------------------------------------------------
+extern __device__ int g_device_error;
+
+enum DeviceError : int {
+  kErrNone = 0,
+  kErrTimeoutGemmProducer = 0x101,
+  kErrTimeoutGemmMma = 0x102,
+  kErrTimeoutGemmEpilogue = 0x103,
+  kErrTimeoutAttention = 0x201,
+  kErrBadIndex = 0x301,
+  kErrBadAlignment = 0x302,
+};
+
+// a wait that has not completed after this long is treated as a hang
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+MORJ_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+MORJ_DEV void report(int code) { atomicCAS(&g_device_error, 0, code); }
+
+MORJ_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------------------------------------------
+MORJ_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+MORJ_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+MORJ_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+MORJ_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+MORJ_DEV bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with `parity` to complete. Returns false (after reporting `code` and raising `*abort`) when
+// the wait runs past the limit, or as soon as another thread of the CTA raised `*abort`.
+MORJ_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        report(code);
+        return false;
+      }
+    }
+  }
+}
+
+// Wait for a phase on the exit path (copies or MMAs this CTA issued must finish before it frees its resources):
+// bounded, and independent of the abort flag.
+MORJ_DEV bool mbar_wait_landed(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 63) == 63 && global_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// TMA (tiled, no multicast anywhere in this library)
+// ---------------------------------------------------------------------------------------------------------------
+MORJ_DEV void tma_prefetch(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+MORJ_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+MORJ_DEV uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+MORJ_DEV uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+MORJ_DEV uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+MORJ_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// tcgen05: TMEM allocation, MMA, commit, loads
+// ---------------------------------------------------------------------------------------------------------------
+MORJ_DEV void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
+               : "memory");
+}
+MORJ_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+MORJ_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+MORJ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+MORJ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, BF16 inputs, FP32 accumulator; `accumulate` = 0 overwrites D.
+MORJ_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// the mbarrier receives one arrival once every MMA issued so far by this thread has completed
+MORJ_DEV void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives lane (base + i), columns [col, col + 32)
+MORJ_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+MORJ_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a 128-byte-swizzled tile whose 8-row groups are 1024 bytes apart
+// (K-major operand, or MN-major operand with `lbo` = distance between 64-element column groups).
+MORJ_DEV uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes = 16) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: BF16 x BF16 -> FP32, M x N tile; `b_mn_major` when B is stored N-contiguous.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major = false) {
+  return (1u << 4)                      // D format: FP32
+         | (1u << 7)                    // A format: BF16
+         | (1u << 10)                   // B format: BF16
+         | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(N >> 3) << 17)   // N / 8
+         | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+// byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128-byte-swizzled [rows x 128 B] block
+MORJ_DEV uint32_t sw128_offset(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// numerics helpers
+// ---------------------------------------------------------------------------------------------------------------
+MORJ_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
+MORJ_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+MORJ_DEV float2 unpack_bf16x2(uint32_t v) {
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+  return __bfloat1622float2(b);
+}
+
+// tanh-approximated GELU from its definition 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+MORJ_DEV float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float inner = k0 * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+// host side: status and the calling thread's last error message (rowops.cu)
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+}  // namespace morj

@@ -1,0 +1,341 @@
+// BF16 projection GEMM for sm_100a: C = A . B^T with FP32 accumulation in TMEM.
+//
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0      TMA producer: A [128 x 64] and B [256 x 64] tiles (128-byte swizzle) into a 4-stage ring
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator, commits each
+//               stage back to the producer and each finished tile to the epilogue
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (thread = row), BF16 rounding and the fused epilogue
+// Two 256-column accumulators (all 512 TMEM columns) let the epilogue of tile i overlap the main loop of i+1.
+// Tiles are walked in groups of 16 row-blocks so the activation slice and the weight tiles of the CTAs in flight
+// stay in L2. No TMA multicast is used, so the kernel is valid whichever GPU's memory the pointers refer to.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace morj {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int THREADS = 192;
+constexpr int GROUP_M = 16;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+
+struct TileCoord {
+  int m, n;
+};
+
+MORJ_DEV TileCoord tile_coord(int t, int num_m, int num_n) {
+  const int per_group = GROUP_M * num_n;
+  const int group = t / per_group;
+  const int first_m = group * GROUP_M;
+  const int gm = min(GROUP_M, num_m - first_m);
+  const int local = t - group * per_group;
+  return {first_m + local % gm, local / gm};
+}
+
+template <int EPI>
+MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv_bfloat16* C, long long ldc, int N) {
+  if constexpr (EPI == MORJ_EPI_STORE) {
+    __nv_bfloat16* crow = C + (size_t)row * ldc;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tacc + c, r);
+      tmem_wait_ld();
+      const int col = n_blk * BN + c;
+      if (row_ok && col < N) {
+        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          if (col + v * 8 < N) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+            pk.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+            pk.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+            pk.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+            dst[v] = pk;
+          }
+        }
+      }
+    }
+  } else {
+    // gate columns [0, 128), up columns [128, 256) of this tile -> 128 outputs
+    const int F = N / 2;
+    __nv_bfloat16* crow = C + (size_t)row * ldc;
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tacc + c, g);
+      tmem_ld32(tacc + BN / 2 + c, u);
+      tmem_wait_ld();
+      const int col = n_blk * (BN / 2) + c;
+      if (row_ok && col < F) {
+        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float gv = bf16_round(__uint_as_float(g[v * 8 + e]));
+            const float uv = bf16_round(__uint_as_float(u[v * 8 + e]));
+            o[e] = gelu_tanh(gv) * uv;
+          }
+          uint4 pk;
+          pk.x = pack_bf16x2(o[0], o[1]);
+          pk.y = pack_bf16x2(o[2], o[3]);
+          pk.z = pack_bf16x2(o[4], o[5]);
+          pk.w = pack_bf16x2(o[6], o[7]);
+          dst[v] = pk;
+        }
+      }
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
+  const uint32_t done0 = smem_u32(bars + 2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 128);
+    }
+    mbar_init(done0, 1);
+    *abort = 0;
+    fence_mbar_init();
+    tma_prefetch(&map_a);
+    tma_prefetch(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + BK - 1) / BK;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_normal();
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+        const TileCoord tc = tile_coord(t, num_m, num_n);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kErrTimeoutGemmProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_base + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(full0 + 8 * stage, STAGE_BYTES);
+          tma_load_2d(sa, &map_a, full0 + 8 * stage, kb * BK, tc.m * BM, pol_a);
+          tma_load_2d(sa + A_BYTES, &map_b, full0 + 8 * stage, kb * BK, tc.n * BN, pol_b);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // no copy may still be in flight when the CTA exits: wait for the last fills to land
+      const int pending = issued < STAGES ? issued : STAGES;
+      for (int j = 1; j <= pending; ++j) {
+        const int s = (stage - j + STAGES) % STAGES;
+        const uint32_t ph = (stage - j >= 0) ? phase : (phase ^ 1);
+        mbar_wait_landed(full0 + 8 * s, ph);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kErrTimeoutGemmMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, abort, kErrTimeoutGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16(d_tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), IDESC, (kb | k) != 0);
+          }
+          umma_commit(empty0 + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(accf0 + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // TMEM is freed below only after every MMA issued here has completed
+      umma_commit(done0);
+      mbar_wait_landed(done0, 0);
+    }
+  } else {
+    // epilogue warps 2..5: warp w reads TMEM lanes 32 * (w % 4) .. + 31
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const TileCoord tc = tile_coord(t, num_m, num_n);
+      // lane 0 waits for the accumulator; the warp follows its verdict (tcgen05.ld below is warp-collective)
+      int ok = lane == 0 ? (int)mbar_wait(accf0 + 8 * acc, acc_phase, abort, kErrTimeoutGemmEpilogue) : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = tc.m * BM + quarter * 32 + lane;
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      epilogue_tile<EPI>(tacc, row, tc.n, row < M, C, ldc, N);
+      tc_fence_before();
+      mbar_arrive(acce0 + 8 * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2D BF16 tensor map over a row-major [rows, cols] matrix with leading dimension ld, box [box_rows, 64 cols].
+static int make_map(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(MORJ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MORJ_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MORJ_OK;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int EPI>
+static int launch(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
+                  int K, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, A, M, K, lda, BM);
+  if (st) return st;
+  st = make_map(&mb, B, N, K, ldb, BN);
+  if (st) return st;
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K);
+  return check_launch("gemm_kernel");
+}
+
+}  // namespace gemm
+}  // namespace morj
+
+extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc,
+                              int M, int N, int K, int epilogue, void* stream) {
+  using namespace morj;
+  if (M == 0 || N == 0) return MORJ_OK;
+  if (!A || !B || !C || M < 0 || N < 0 || K <= 0)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: bad pointers or sizes (M=%d N=%d K=%d)", M, N, K);
+  if (K % 8 || lda % 8 || ldb % 8 || ldc % 8 || lda < K || ldb < K)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: K and leading dimensions must be multiples of 8 (K=%d)", K);
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: pointers must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (epilogue == MORJ_EPI_STORE) {
+    if (N % 16 || ldc < N) return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: N must be a multiple of 16 (N=%d)", N);
+    return gemm::launch<MORJ_EPI_STORE>(A, lda, B, ldb, C, ldc, M, N, K, s);
+  }
+  if (epilogue == MORJ_EPI_GEGLU) {
+    if (N % gemm::BN || ldc < N / 2)
+      return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: GEGLU needs N a multiple of 256 (N=%d)", N);
+    return gemm::launch<MORJ_EPI_GEGLU>(A, lda, B, ldb, C, ldc, M, N, K, s);
+  }
+  return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: unknown epilogue %d", epilogue);
+}

@@ -1,0 +1,332 @@
+"""Tree-prefill throughput on B200: the lean engine's forward over a token tree at the 31B-class BF16 config.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload text|multimodal|latency]
+
+One step = one forward pass over one request tree (every tree token computed, 60 layers, label probabilities at the
+end). `value` is device-timed tokens/s with the plan tables already resident in HBM (CUDA events over K steps, max
+over ranks); `e2e` is the same metric through the engine's public call `LeanGemma4.run` from host token ids to host
+probabilities (planning, host-to-device tables, kernels, device-to-host probabilities inside the timed region).
+N > 1: one process per GPU, each a full model replica on its own seeded tree (independent trees: no collective on
+the data path; weak scaling). Weights (~52 GB BF16) and every input are larger than L2, so no L2 flush is needed.
+
+`--impl reference` times the reference lean path on the host CPU (its restatement in `oracle/lean_oracle.py`: the
+reference has no CPU implementation of its GPU path) on the same workload: one sliding and one global decoder layer
+at the full token count, extrapolated to the 60-layer pattern.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'tree-prefill tokens/s per B200 at 31B BF16'
+UNIT = 'tokens/s'
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, 'MEASURED_PEAKS.json')) as f:
+            p = json.load(f)
+        return dict(hbm=p['hbm_gbs'], bf16=p['bf16_tflops'], bf16_sustained=p['bf16_tflops_sustained'],
+                    source='measured')
+    except (OSError, KeyError, ValueError):
+        return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source='fallback')
+
+
+def workload(name, rank):
+    from morj_b200 import workloads as w
+    if name == 'text':
+        return w.text_tree(seed=rank), 'text tree: 1500-token prefix + 3 questions x 3 rotations x 60 tokens'
+    if name == 'latency':
+        return w.latency_tree(seed=rank), 'latency tree: 8192-token prefix + 8 branches x 64 tokens'
+    if name == 'multimodal':
+        return (w.multimodal_tree(seed=rank),
+                'multimodal tree: 8 x 560 image soft tokens + 300 text + 2 questions x 4 rotations x 40 tokens')
+    raise ValueError(name)
+
+
+class Clocks:
+    """nvidia-smi samples of this process's GPU while a region runs."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_id):
+        self.gpu_id, self.proc, self.rows = gpu_id, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200', '-i', self.gpu_id], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(',')]
+            if len(parts) == 9:
+                self.rows.append(parts)
+
+    def summary(self):
+        if not self.rows:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace('.', '').isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace('.', '').isdigit()]
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == 'active'})
+        power = [float(r[3]) for r in self.rows if r[3].replace('.', '').isdigit()]
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(mx) if mx else None,
+                'reasons': reasons, 'samples': len(self.rows), 'power_w_max': max(power) if power else None}
+
+
+def cpu_layer_baseline(n_layers_pattern, budget_s=30.0):
+    """The reference lean path's per-layer work on the host CPU (the oracle in BF16, torch on every host thread):
+    one sliding and one global decoder layer at the text tree's full token count, extrapolated to the 60-layer
+    pattern (50 sliding + 10 global); embedding and readout are < 0.01% of the FLOPs and left out."""
+    import torch
+    from morj_b200 import workloads as w
+    from morj_b200.tree import Tree
+    from oracle.lean_oracle import OracleModel, rope_tables
+    torch.set_num_threads(os.cpu_count())
+    top = w.gemma31b_config()
+    cfg = dict(top['text_config'])
+    cfg['layer_types'] = ['sliding_attention', 'full_attention']
+    cfg['num_hidden_layers'] = 2
+    small = dict(top, text_config=dict(cfg, vocab_size=16))
+    from morj_b200.checkpoint import tensor_shapes
+    # timing only: weights are a tiled seeded random block (values do not change the work)
+    block = (torch.randn(1 << 22, generator=torch.Generator().manual_seed(0)) * 0.02).to(torch.bfloat16)
+    state = {}
+    for k, shape in tensor_shapes(small):
+        n = int(np.prod(shape))
+        reps = -(-n // block.numel())
+        t = block.repeat(reps)[:n].reshape(shape).clone()
+        if len(shape) == 1:
+            t = torch.ones(shape, dtype=torch.bfloat16)
+        state[k] = t
+    model = OracleModel(small, state)
+    tree_in = w.text_tree(0)
+    tree = Tree(tree_in['seqs'])
+    need = tree.pass_nodes(range(len(tree.seqs)), set())
+    plan = tree.plan_pass(need, list(range(len(tree.seqs))), cfg['sliding_window'], 16384, 8192, False)
+    st = plan['steps'][0]
+    n = len(st['tokens'])
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(n, cfg['hidden_size'], generator=g).to(torch.bfloat16).float()
+    h = x.clone()
+    rope = {k: rope_tables(st['positions'], v) for k, v in model.inv.items()}
+
+    def one(i):
+        t0 = time.perf_counter()
+        model.layer(i, x, h, st, plan['cap'], rope, None, 'bf16')
+        return time.perf_counter() - t0
+    t_s, t_g = one(0), one(1)  # warm-up
+    runs = 3 if (t_s + t_g) * 3 < budget_s else 1
+    ts, tg = [], []
+    for _ in range(runs):
+        ts.append(one(0))
+        tg.append(one(1))
+    sl = sum(1 for k in w.gemma31b_config()['text_config']['layer_types'] if k == 'sliding_attention')
+    gl = n_layers_pattern - sl
+    per_tree = sl * statistics.median(ts) + gl * statistics.median(tg)
+    return dict(tokens=n, seconds_per_tree=per_tree, sliding_s=statistics.median(ts), global_s=statistics.median(tg),
+                runs=runs, cores=os.cpu_count(), cpu=_cpu_model())
+
+
+def _cpu_model():
+    try:
+        with open('/proc/cpuinfo') as f:
+            for line in f:
+                if line.startswith('model name'):
+                    return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    steps, vals = [], []
+    for i in range(args.warmup + args.steps):
+        r = cpu_layer_baseline(60, budget_s=20.0)
+        if i >= args.warmup:
+            steps.append(r)
+            vals.append(r['tokens'] / r['seconds_per_tree'])
+    r = steps[-1]
+    value = r['tokens'] * len(vals) / sum(s['seconds_per_tree'] for s in steps)
+    line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=1000 * r['seconds_per_tree'], higher_is_better=True, scaling='weak', vs_baseline=None,
+                dtype='bf16', data='synthetic', impl='reference',
+                config=dict(workload='31B-class text tree (1500 + 9 x 60 tokens), CPU, layer-extrapolated',
+                            tokens=r['tokens'], l2='inputs larger than L2'),
+                cpu_baseline=dict(value=value, unit=UNIT, cores=r['cores'], kind='port',
+                                  sample=('one sliding + one global decoder layer at the full 2040-token tree '
+                                          'through oracle/lean_oracle.py (BF16, torch CPU), extrapolated x50 + x10'),
+                                  cpu=r['cpu']),
+                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency'])
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    if args.impl == 'reference':
+        return reference_arm(args, rank, world)
+
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from morj_b200 import workloads as w
+    from morj_b200.lean_core import LeanGemma4
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    top = w.gemma31b_config()
+    t_init = time.perf_counter()
+    model = LeanGemma4.random_init(top, seed=0, device=dev)
+    torch.cuda.synchronize()
+    init_s = time.perf_counter() - t_init
+    tree_in, desc = workload(args.workload, rank)
+    images = [f.to(dev) for f in tree_in['images']] if tree_in['images'] else None
+    seqs = list(range(len(tree_in['seqs'])))
+    req = model.prepare(tree_in['seqs'], tree_in['label_ids'], images=images)
+    prepared = model.prepare_pass(req, seqs)
+    tokens = prepared['tokens']
+    flops_lin = w.linear_flops_per_token(top) * tokens
+    pairs = w.attention_pairs(prepared['plan'], top['text_config']['sliding_window'], top['text_config']['layer_types'])
+    c = top['text_config']
+    flops_attn = 4 * c['num_attention_heads'] * c['head_dim'] * pairs
+    props = torch.cuda.get_device_properties(dev)
+    clocks = Clocks('GPU-' + str(props.uuid) if hasattr(props, 'uuid') else str(local))
+
+    # ---- device-timed forward over a resident plan -------------------------------------------------------------
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model.execute_pass(prepared)
+        barrier()
+        clocks.start()
+        launches0 = model.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record()
+        for _ in range(args.steps):
+            model.execute_pass(prepared)
+        e1.record()
+        barrier()
+        ms = e0.elapsed_time(e1) / args.steps
+        launches = (model.launches - launches0) // args.steps
+        # ---- end to end through the public call (host ids -> host probabilities) --------------------------------
+        for _ in range(2):
+            model.run(req, seqs)
+        barrier()
+        lat = []
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record()
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            model.run(req, seqs)
+            lat.append(1000 * (time.perf_counter() - t0))
+        e3.record()
+        barrier()
+        clocks.stop()
+        e2e_ms = e2.elapsed_time(e3) / args.steps
+        h2d, d2h = model.h2d_bytes, model.d2h_bytes
+        # ---- one traced step (CUDA events around every kernel) for the per-kernel roofline -----------------------
+        model.trace = []
+        model.execute_pass(prepared)
+        torch.cuda.synchronize()
+        trace, model.trace = model.trace, None
+    per_kind = {}
+    for kind, fl, a, b in trace:
+        d = per_kind.setdefault(kind, dict(ms=0.0, launches=0, flops=0))
+        d['ms'] += a.elapsed_time(b)
+        d['launches'] += 1
+        d['flops'] += fl
+    ms_max = max_over_ranks(ms)
+    e2e_max = max_over_ranks(e2e_ms)
+    value = tokens * world / (ms_max / 1000)
+    e2e_value = tokens * world / (e2e_max / 1000)
+    pk = peaks()
+    g = per_kind.get('gemm', dict(ms=1.0, launches=1, flops=0))
+    achieved = g['flops'] / (g['ms'] / 1000) / 1e12
+    traffic = None
+    tfile = os.path.join(ROOT, 'profiles', 'gemm_traffic.json')
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            traffic = json.load(f).get('bytes_per_launch')
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r = cpu_layer_baseline(60)
+            cpu = dict(value=r['tokens'] / r['seconds_per_tree'], unit=UNIT, cores=r['cores'], kind='port',
+                       sample=(f"one sliding ({r['sliding_s']:.2f} s) + one global ({r['global_s']:.2f} s) decoder "
+                               f"layer at the full {r['tokens']}-token tree through oracle/lean_oracle.py (BF16, torch "
+                               f"CPU, median of {r['runs']}), extrapolated x50 + x10"), cpu=r['cpu'])
+        except Exception as error:  # the baseline must not take the GPU number down with it
+            cpu = dict(value=None, unit=UNIT, cores=os.cpu_count(), kind='port', sample=f'failed: {error}')
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=ms_max, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
+            data='synthetic (seeded random-init weights N(0, 0.02), uniform token ids)',
+            config=dict(workload=f'31B-class Gemma-style decoder, {desc}', tokens=tokens,
+                        parallelism=f'replicas x{world} (independent trees, no collective)',
+                        l2='inputs larger than L2 (52 GB of weights streamed per step)',
+                        tflops_per_tree_specified=round((flops_lin + flops_attn) / 1e12, 2)),
+            model_tflops=round((flops_lin + flops_attn) / (ms_max / 1000) / 1e12, 1),
+            p50_tree_latency_ms=round(statistics.median(lat), 3),
+            roofline=dict(bound='tensor', kernel='morj gemm_kernel (tcgen05 BF16)', achieved=round(achieved, 1),
+                          peak=pk['bf16_sustained'], unit='TFLOP/s', frac=round(achieved / pk['bf16_sustained'], 4),
+                          traffic=traffic, peak_source=f"{pk['source']} sustained cuBLAS BF16",
+                          launches=g['launches'], avg_launch_us=round(1000 * g['ms'] / max(g['launches'], 1), 2)),
+            breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
+            e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
+                     ms_per_step=e2e_max),
+            gpu_launches=int(launches * args.steps),
+            clocks=clocks.summary(), init_s=round(init_s, 1))
+        if cpu is not None:
+            line['cpu_baseline'] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

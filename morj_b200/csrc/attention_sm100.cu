@@ -209,8 +209,9 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
       umma_commit(bar_s);
     }
-    int ok = lane == 0 ? (int)mbar_wait(bar_s, ci & 1, abort, kErrTimeoutAttention) : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
+    // every warp's lane 0 waits; the CTA acts on one verdict so no thread is left at a barrier alone
+    int ok = lane == 0 ? (int)mbar_wait(bar_s, ci & 1, abort, kErrTimeoutAttention) : 1;
+    ok = __syncthreads_and(ok);
     if (!ok) {
       failed = true;
       break;
@@ -266,8 +267,8 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
       umma_commit(bar_o);
     }
-    ok = lane == 0 ? (int)mbar_wait(bar_o, ci & 1, abort, kErrTimeoutAttention) : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
+    ok = lane == 0 ? (int)mbar_wait(bar_o, ci & 1, abort, kErrTimeoutAttention) : 1;
+    ok = __syncthreads_and(ok);
     if (!ok) {
       failed = true;
       break;

@@ -150,10 +150,21 @@ class LeanGemma4:
         return self
 
     @classmethod
-    def random_init(cls, top, seed=0, device='cuda', std=0.02, norm_std=0.1, **kw):
-        """An engine over seeded random-init weights generated on `device` (no checkpoint on disk)."""
-        gen = dict(iter_random_state(top, seed=seed, std=std, norm_std=norm_std, device=device))
-        return cls.from_state(top, gen, device=device, **kw)
+    def random_init(cls, top, seed=0, device='cuda', std=0.02, norm_std=0.1, retain_budget_gb=10.0,
+                    single_max=16384, step_tokens=8192):
+        """An engine over seeded random-init weights generated on `device` (no checkpoint on disk); tensors are drawn
+        in checkpoint order and handed over one at a time, so the peak memory is the model plus one layer."""
+        gen = iter_random_state(top, seed=seed, std=std, norm_std=norm_std, device=device)
+        cache = {}
+
+        def get(key):
+            while key not in cache:
+                k, t = next(gen)
+                cache[k] = t
+            return cache.pop(key)
+        self = cls.__new__(cls)
+        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens)
+        return self
 
     def _setup(self, top, get, device, retain_budget_gb, single_max, step_tokens):
         cfg = top['text_config']
@@ -217,6 +228,8 @@ class LeanGemma4:
         self.gpu_ms = 0.0
         self.last_need = []
         self.h2d_bytes = 0
+        self.launches = 0
+        self.trace = None
         self.free_bytes = (torch.cuda.mem_get_info(self.device)[0] - (3 << 30)) if self.device.type == 'cuda' else 0
         hd = max(dd for _, dd in self.geom.values())
         qkv_rows = max(l['qkv'].shape[0] for l in self.layers)
@@ -280,7 +293,7 @@ class LeanGemma4:
     def _gather(self, src, idx):
         width = src[0].numel()
         out = torch.empty((len(idx),) + tuple(src.shape[1:]), dtype=src.dtype, device=self.device)
-        nat.call('morj_gather_rows', src.data_ptr(), width, idx.data_ptr(), len(idx), width, out.data_ptr(), width,
+        self._k('rows', 'morj_gather_rows', src.data_ptr(), width, idx.data_ptr(), len(idx), width, out.data_ptr(), width,
                  self._stream())
         return out
 
@@ -347,14 +360,13 @@ class LeanGemma4:
                 step //= 2
         return need, head, pinned, plan
 
-    @torch.inference_mode()
-    def run(self, req, seqs, available=None):
-        """Label probabilities for sequences `seqs` of `req`, computing only the nodes not cached yet
-        (reference `lean_core.py:495-576`: the same planning, memory-fit loop, pool strategy and state updates)."""
+    def prepare_pass(self, req, seqs, available=None):
+        """Host half of `run`: plan (with the memory-fit loop), the pools the pass writes (retained, pinned, per-pass,
+        or per-step temporaries), and every step's tables uploaded to the device. The result can be executed any
+        number of times (`execute_pass`); each execution recomputes the same nodes into the same slots."""
         tree = req.tree
         t0 = time.perf_counter()
         need, head, pinned, plan = self.plan(req, seqs, available)
-        self.last_need = need
         multi = len(plan['steps']) > 1
         if req.retain:
             pools = req.pools
@@ -373,13 +385,34 @@ class LeanGemma4:
         labels = [req.label_ids[b] for b in seqs]
         if any(len(ids) > MAX_LABELS for ids in labels):
             raise ValueError(f'at most {MAX_LABELS} labels per sequence')
-        self.timing = {'host_setup_ms': 1000 * (time.perf_counter() - t0), 'steps': len(plan['steps']),
-                       'tokens': sum(len(st['tokens']) for st in plan['steps'])}
         self.h2d_bytes = 0
+        tables = [self._step_tables(k, st, plan, req) for k, st in enumerate(plan['steps'])]
+        ro = self._readout_tables(plan, labels)
+        host_ms = 1000 * (time.perf_counter() - t0)
+        return dict(req=req, seqs=list(seqs), need=need, head=head, pinned=pinned, plan=plan, pools=pools,
+                    labels=labels, tables=tables, ro=ro, host_ms=host_ms, h2d_bytes=self.h2d_bytes,
+                    tokens=sum(len(st['tokens']) for st in plan['steps']))
+
+    def execute_pass(self, p):
+        """Device half of `run`: every step's forward and the label head; returns the FP32 probabilities (device,
+        CSR over the requested sequences' labels). Launches only; nothing waits for the GPU."""
+        plan = p['plan']
+        finals = [self._step(k, st, plan, p['pools'], p['head'], p['req'], p['tables'][k])
+                  for k, st in enumerate(plan['steps'])]
+        return self._readout(finals, p['ro'])
+
+    @torch.inference_mode()
+    def run(self, req, seqs, available=None):
+        """Label probabilities for sequences `seqs` of `req`, computing only the nodes not cached yet
+        (reference `lean_core.py:495-576`: the same planning, memory-fit loop, pool strategy and state updates)."""
+        tree = req.tree
+        p = self.prepare_pass(req, seqs, available)
+        self.last_need = p['need']
+        plan, pinned, labels = p['plan'], p['pinned'], p['labels']
+        self.timing = {'host_setup_ms': p['host_ms'], 'steps': len(plan['steps']), 'tokens': p['tokens']}
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        finals = [self._step(k, st, plan, pools, head, req) for k, st in enumerate(plan['steps'])]
-        probs = self._readout(finals, plan['readout'], labels)
+        probs = self.execute_pass(p)
         end.record()
         self.enqueued = time.perf_counter()  # host done launching; the copy below waits for the GPU
         flat = probs.cpu().numpy()
@@ -395,7 +428,7 @@ class LeanGemma4:
         self.timing['gpu_ms'] = self.gpu_ms
         req.read.update(seqs)
         if req.retain or req.pinned:
-            req.computed.update(need)
+            req.computed.update(p['need'])
         if req.pinned:
             req.tables = {}
             for kk in 'gs':
@@ -404,29 +437,46 @@ class LeanGemma4:
                 req.tables[kk] = table
         return out
 
-    def _readout(self, finals, readout, labels):
-        """Final norm + label rows + softcap + per-sequence softmax in one kernel (reference `lean_core.py:558-561`)."""
-        H = self.hidden
-        base, xs, total = [], [], 0
-        for xr, rows in finals:
-            base.append((total, {r: j for j, r in enumerate(rows)}))
-            if rows:
-                xs.append(xr)
-            total += len(rows)
-        x_all = xs[0] if len(xs) == 1 else torch.cat(xs)
-        seq_row = [base[k][0] + base[k][1][r] for k, r in readout]
-        indptr = np.concatenate([[0], np.cumsum([len(ids) for ids in labels])])
+    def _readout_tables(self, plan, labels):
+        """Per requested sequence: its row among the readout rows of all steps (in step order) and its label CSR."""
+        offset, pos = 0, {}
+        for k in range(len(plan['steps'])):
+            rows = sorted({r for kk, r in plan['readout'] if kk == k})
+            for j, r in enumerate(rows):
+                pos[(k, r)] = offset + j
+            offset += len(rows)
         t = _Tables(self.device)
-        t.add('seq_row', seq_row)
+        t.add('seq_row', [pos[(k, r)] for k, r in plan['readout']])
+        indptr = np.concatenate([[0], np.cumsum([len(ids) for ids in labels])])
         t.add('indptr', indptr)
         t.add('labels', np.concatenate([np.asarray(ids, dtype=np.int64) for ids in labels]))
         t.upload()
         self.h2d_bytes += t.nbytes
-        probs = torch.empty(int(indptr[-1]), dtype=torch.float32, device=self.device)
-        nat.call('morj_label_head', x_all.data_ptr(), H, t.ptr('seq_row'), t.ptr('indptr'), t.ptr('labels'),
-                 len(labels), self.norm.data_ptr(), self.embed.data_ptr(), H, self.eps, self.softcap,
-                 probs.data_ptr(), self._stream())
+        return dict(t=t, n_seq=len(labels), n_labels=int(indptr[-1]))
+
+    def _readout(self, finals, ro):
+        """Final norm + label rows + softcap + per-sequence softmax in one kernel (reference `lean_core.py:558-561`)."""
+        H = self.hidden
+        xs = [xr for xr, rows in finals if rows]
+        x_all = xs[0] if len(xs) == 1 else torch.cat(xs)
+        t = ro['t']
+        probs = torch.empty(ro['n_labels'], dtype=torch.float32, device=self.device)
+        self._k('head', 'morj_label_head', x_all.data_ptr(), H, t.ptr('seq_row'), t.ptr('indptr'), t.ptr('labels'),
+                ro['n_seq'], self.norm.data_ptr(), self.embed.data_ptr(), H, self.eps, self.softcap,
+                probs.data_ptr(), self._stream())
         return probs
+
+    def _k(self, kind, name, *args, flops=0):
+        """Launch one native kernel; with `trace` on, bracket it with CUDA events (for per-kernel timing)."""
+        self.launches += 1
+        if self.trace is None:
+            nat.call(name, *args)
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        nat.call(name, *args)
+        e1.record()
+        self.trace.append((kind, flops, e0, e1))
 
     # ---- forward over one step ------------------------------------------------------------------------------------
     def _work(self, qo, G):
@@ -495,20 +545,20 @@ class LeanGemma4:
         M, K = a.shape
         N = w.shape[0] if w_rows is None else w_rows
         wp = w.data_ptr() + w_offset_rows * w.stride(0) * w.element_size()
-        nat.call('morj_gemm_bf16', a.data_ptr(), a.stride(0), wp, w.stride(0), out.data_ptr(), out.stride(0), M, N, K,
-                 epi, self._stream())
+        self._k('gemm', 'morj_gemm_bf16', a.data_ptr(), a.stride(0), wp, w.stride(0), out.data_ptr(), out.stride(0),
+                M, N, K, epi, self._stream(), flops=2 * M * N * K)
 
     def _attention(self, q, k_pool, v_pool, out, t, qo, kv_indptr, kv_indices, n_seg, n_bidir, kind, work, n_work):
         hk, d = self.geom[kind]
         window = self.window if kind == 'sliding_attention' else 0
-        nat.call('morj_tree_attention', q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), out.data_ptr(),
+        self._k('attention', 'morj_tree_attention', q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), out.data_ptr(),
                  t.ptr(qo), t.ptr(kv_indptr), t.ptr(kv_indices), None, n_seg, n_bidir, self.hq, hk, d, 1, window,
                  1.0, t.ptr(work), n_work, self._stream())
 
-    def _step(self, k, st, plan, pools, head, req):
+    def _step(self, k, st, plan, pools, head, req, tables):
         """One forward over a planned step (reference `lean_core.py:599-694`); returns (the residual rows of the
         step's readout tokens after the last layer, their row indices in the step)."""
-        t, rows, n_work = self._step_tables(k, st, plan, req)
+        t, rows, n_work = tables
         s = self._stream()
         n = len(st['tokens'])
         H, eps, hq = self.hidden, self.eps, self.hq
@@ -518,7 +568,7 @@ class LeanGemma4:
         x = torch.empty(n, H, dtype=bf, device=dev)
         h = torch.empty(n, H, dtype=bf, device=dev)
         feat = req.features
-        nat.call('morj_embed_rmsnorm', t.ptr('tokens'), t.ptr('feature_row') if feat is not None else None,
+        self._k('rows', 'morj_embed_rmsnorm', t.ptr('tokens'), t.ptr('feature_row') if feat is not None else None,
                  _ptr(feat), self.embed.data_ptr(), n, H, self.embed_scale, self.layers[0]['in_ln'].data_ptr(), eps,
                  x.data_ptr(), h.data_ptr(), s)
         temp = {}
@@ -551,7 +601,7 @@ class LeanGemma4:
             qkv_i = qkv[:, :nq]
             self._gemm(h, layer['qkv'], qkv_i)
             q_i = q[:, :hq * d]
-            nat.call('morj_qkv_post', qkv_i.data_ptr(), qkv.stride(0), n, hq, hk, has_v, d,
+            self._k('rows', 'morj_qkv_post', qkv_i.data_ptr(), qkv.stride(0), n, hq, hk, has_v, d,
                      layer['q_norm'].data_ptr(), layer['k_norm'].data_ptr(), t.ptr('positions'),
                      self.inv_freq[kind].data_ptr(), t.ptr('slots_' + kk), eps, q_i.data_ptr(), k_pool.data_ptr(),
                      v_pool.data_ptr(), s)
@@ -559,18 +609,18 @@ class LeanGemma4:
             self._attention(q_i, k_pool, v_pool, a_i, t, 'qo', 'kv_indptr_' + kk, 'kv_indices_' + kk, n_seg,
                             nb if kind == 'sliding_attention' else 0, kind, 'work_' + kk, n_work[kk])
             self._gemm(a_i, layer['o'], o)
-            nat.call('morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_attn'].data_ptr(),
+            self._k('rows', 'morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_attn'].data_ptr(),
                      layer['pre_ff'].data_ptr(), n, H, eps, s)
             self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
             self._gemm(act, layer['down'], o)
             nxt = self.layers[i + 1]['in_ln'] if i < last else layer['in_ln']
-            nat.call('morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_ff'].data_ptr(),
+            self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_ff'].data_ptr(),
                      layer['scalar'].data_ptr(), nxt.data_ptr(), n, H, eps, int(i < last), s)
         # (no pruning) the readout rows' residual stream
         if not rows:
             return None, []
         xr = torch.empty(len(rows), H, dtype=bf, device=dev)
-        nat.call('morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), len(rows), H, xr.data_ptr(), H, s)
+        self._k('rows', 'morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), len(rows), H, xr.data_ptr(), H, s)
         return xr, rows
 
     def _last_layer(self, t, rows, n_work, layer, h, x, k_pool, v_pool, kind, has_v):
@@ -586,18 +636,18 @@ class LeanGemma4:
         kvw = layer['qkv'].shape[0] - qd
         kv = torch.empty(n, kvw, dtype=bf, device=dev)
         self._gemm(h, layer['qkv'], kv, w_rows=kvw, w_offset_rows=qd)
-        nat.call('morj_qkv_post', kv.data_ptr(), kvw, n, 0, hk, has_v, d, layer['q_norm'].data_ptr(),
+        self._k('rows', 'morj_qkv_post', kv.data_ptr(), kvw, n, 0, hk, has_v, d, layer['q_norm'].data_ptr(),
                  layer['k_norm'].data_ptr(), t.ptr('positions'), self.inv_freq[kind].data_ptr(), t.ptr('slots_' + kk),
                  eps, None, k_pool.data_ptr(), v_pool.data_ptr(), s)
         if not rows:
             return None, []
         R = len(rows)
         hr = torch.empty(R, H, dtype=bf, device=dev)
-        nat.call('morj_gather_rows', h.data_ptr(), H, t.ptr('ro_rows'), R, H, hr.data_ptr(), H, s)
+        self._k('rows', 'morj_gather_rows', h.data_ptr(), H, t.ptr('ro_rows'), R, H, hr.data_ptr(), H, s)
         q_lin = torch.empty(R, qd, dtype=bf, device=dev)
         self._gemm(hr, layer['qkv'], q_lin, w_rows=qd)
         q = torch.empty(R, qd, dtype=bf, device=dev)
-        nat.call('morj_qkv_post', q_lin.data_ptr(), qd, R, hq, 0, has_v, d, layer['q_norm'].data_ptr(),
+        self._k('rows', 'morj_qkv_post', q_lin.data_ptr(), qd, R, hq, 0, has_v, d, layer['q_norm'].data_ptr(),
                  layer['k_norm'].data_ptr(), t.ptr('ro_positions'), self.inv_freq[kind].data_ptr(), None, eps,
                  q.data_ptr(), None, None, s)
         attn = torch.empty(R, qd, dtype=bf, device=dev)
@@ -606,15 +656,15 @@ class LeanGemma4:
         o = torch.empty(R, H, dtype=bf, device=dev)
         self._gemm(attn, layer['o'], o)
         xr = torch.empty(R, H, dtype=bf, device=dev)
-        nat.call('morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), R, H, xr.data_ptr(), H, s)
+        self._k('rows', 'morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), R, H, xr.data_ptr(), H, s)
         h2 = torch.empty(R, H, dtype=bf, device=dev)
-        nat.call('morj_attn_epilogue', o.data_ptr(), xr.data_ptr(), h2.data_ptr(), layer['post_attn'].data_ptr(),
+        self._k('rows', 'morj_attn_epilogue', o.data_ptr(), xr.data_ptr(), h2.data_ptr(), layer['post_attn'].data_ptr(),
                  layer['pre_ff'].data_ptr(), R, H, eps, s)
         F = layer['gu'].shape[0] // 2
         act = torch.empty(R, F, dtype=bf, device=dev)
         self._gemm(h2, layer['gu'], act, nat.EPI_GEGLU)
         self._gemm(act, layer['down'], o)
-        nat.call('morj_mlp_epilogue', o.data_ptr(), xr.data_ptr(), xr.data_ptr(), layer['post_ff'].data_ptr(),
+        self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), xr.data_ptr(), xr.data_ptr(), layer['post_ff'].data_ptr(),
                  layer['scalar'].data_ptr(), layer['in_ln'].data_ptr(), R, H, eps, 0, s)
         return xr, rows
 

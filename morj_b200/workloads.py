@@ -138,3 +138,23 @@ def linear_flops_per_token(top):
             qkv_rows = hq * d + hk * d
         lin += H * qkv_rows + hq * d * H + 2 * F * H + F * H
     return 2 * lin
+
+
+def attention_pairs(plan, window, layer_types):
+    """Visible (query, key) pairs of a pass summed over all layers: a segment's query j sees keys
+    [kv_len - q_len + j - (window - 1), kv_len - q_len + j] on sliding layers and [0, kv_len - q_len + j] on full
+    layers (image blocks are counted as causal here). Attention FLOPs = 4 * Hq * d per pair."""
+    per = {}
+    for kind in ('sliding_attention', 'full_attention'):
+        kk = 's' if kind == 'sliding_attention' else 'g'
+        total = 0
+        for st in plan['steps']:
+            qo = np.asarray(st['qo_indptr'])
+            kp = np.asarray(st['kv_indptr_' + kk])
+            for s in range(len(qo) - 1):
+                ql, kl = int(qo[s + 1] - qo[s]), int(kp[s + 1] - kp[s])
+                hi = kl - ql + np.arange(ql)
+                lo = np.maximum(0, hi - window + 1) if kind == 'sliding_attention' else np.zeros(ql, np.int64)
+                total += int((hi - lo + 1).sum())
+        per[kind] = total
+    return sum(per[k] for k in layer_types)

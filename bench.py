@@ -91,58 +91,67 @@ class Clocks:
                 'reasons': reasons, 'samples': len(self.rows), 'power_w_max': max(power) if power else None}
 
 
-def cpu_layer_baseline(n_layers_pattern, budget_s=30.0):
+class CpuLayers:
     """The reference lean path's per-layer work on the host CPU (the oracle in BF16, torch on every host thread):
-    one sliding and one global decoder layer at the text tree's full token count, extrapolated to the 60-layer
-    pattern (50 sliding + 10 global); embedding and readout are < 0.01% of the FLOPs and left out."""
-    import torch
-    from morj_b200 import workloads as w
-    from morj_b200.tree import Tree
-    from oracle.lean_oracle import OracleModel, rope_tables
-    torch.set_num_threads(os.cpu_count())
-    top = w.gemma31b_config()
-    cfg = dict(top['text_config'])
-    cfg['layer_types'] = ['sliding_attention', 'full_attention']
-    cfg['num_hidden_layers'] = 2
-    small = dict(top, text_config=dict(cfg, vocab_size=16))
-    from morj_b200.checkpoint import tensor_shapes
-    # timing only: weights are a tiled seeded random block (values do not change the work)
-    block = (torch.randn(1 << 22, generator=torch.Generator().manual_seed(0)) * 0.02).to(torch.bfloat16)
-    state = {}
-    for k, shape in tensor_shapes(small):
-        n = int(np.prod(shape))
-        reps = -(-n // block.numel())
-        t = block.repeat(reps)[:n].reshape(shape).clone()
-        if len(shape) == 1:
-            t = torch.ones(shape, dtype=torch.bfloat16)
-        state[k] = t
-    model = OracleModel(small, state)
-    tree_in = w.text_tree(0)
-    tree = Tree(tree_in['seqs'])
-    need = tree.pass_nodes(range(len(tree.seqs)), set())
-    plan = tree.plan_pass(need, list(range(len(tree.seqs))), cfg['sliding_window'], 16384, 8192, False)
-    st = plan['steps'][0]
-    n = len(st['tokens'])
-    g = torch.Generator().manual_seed(1)
-    x = torch.randn(n, cfg['hidden_size'], generator=g).to(torch.bfloat16).float()
-    h = x.clone()
-    rope = {k: rope_tables(st['positions'], v) for k, v in model.inv.items()}
+    one sliding and one global decoder layer of the 31B-class model at the text tree's full token count. A tree costs
+    50 sliding + 10 global layers; embedding and readout are < 0.01% of the FLOPs and left out."""
 
-    def one(i):
+    def __init__(self):
+        import torch
+        from morj_b200 import workloads as w
+        from morj_b200.checkpoint import tensor_shapes
+        from morj_b200.tree import Tree
+        from oracle.lean_oracle import OracleModel, rope_tables
+        torch.set_num_threads(os.cpu_count())
+        top = w.gemma31b_config()
+        cfg = dict(top['text_config'])
+        self.layer_types = list(cfg['layer_types'])
+        cfg['layer_types'] = ['sliding_attention', 'full_attention']
+        cfg['num_hidden_layers'] = 2
+        small = dict(top, text_config=dict(cfg, vocab_size=16))
+        # timing only: weights are a tiled seeded random block (their values do not change the work)
+        block = (torch.randn(1 << 22, generator=torch.Generator().manual_seed(0)) * 0.02).to(torch.bfloat16)
+        state = {}
+        for k, shape in tensor_shapes(small):
+            n = int(np.prod(shape))
+            if len(shape) == 1:
+                state[k] = torch.ones(shape, dtype=torch.bfloat16)
+            else:
+                state[k] = block.repeat(-(-n // block.numel()))[:n].reshape(shape).clone()
+        self.model = OracleModel(small, state)
+        tree_in = w.text_tree(0)
+        tree = Tree(tree_in['seqs'])
+        need = tree.pass_nodes(range(len(tree.seqs)), set())
+        self.plan = tree.plan_pass(need, list(range(len(tree.seqs))), cfg['sliding_window'], 16384, 8192, False)
+        self.st = self.plan['steps'][0]
+        self.tokens = len(self.st['tokens'])
+        g = torch.Generator().manual_seed(1)
+        self.x = torch.randn(self.tokens, cfg['hidden_size'], generator=g).to(torch.bfloat16).float()
+        self.rope = {k: rope_tables(self.st['positions'], v) for k, v in self.model.inv.items()}
+
+    def layer_seconds(self, i):
         t0 = time.perf_counter()
-        model.layer(i, x, h, st, plan['cap'], rope, None, 'bf16')
+        self.model.layer(i, self.x, self.x, self.st, self.plan['cap'], self.rope, None, 'bf16')
         return time.perf_counter() - t0
-    t_s, t_g = one(0), one(1)  # warm-up
-    runs = 3 if (t_s + t_g) * 3 < budget_s else 1
-    ts, tg = [], []
-    for _ in range(runs):
-        ts.append(one(0))
-        tg.append(one(1))
-    sl = sum(1 for k in w.gemma31b_config()['text_config']['layer_types'] if k == 'sliding_attention')
-    gl = n_layers_pattern - sl
-    per_tree = sl * statistics.median(ts) + gl * statistics.median(tg)
-    return dict(tokens=n, seconds_per_tree=per_tree, sliding_s=statistics.median(ts), global_s=statistics.median(tg),
-                runs=runs, cores=os.cpu_count(), cpu=_cpu_model())
+
+    def tree_seconds(self):
+        """One sample: time a sliding and a global layer, extrapolate to the 60-layer pattern."""
+        t_s, t_g = self.layer_seconds(0), self.layer_seconds(1)
+        sl = sum(1 for k in self.layer_types if k == 'sliding_attention')
+        return sl * t_s + (len(self.layer_types) - sl) * t_g, t_s, t_g
+
+
+def cpu_layer_baseline(budget_s=30.0):
+    layers = CpuLayers()
+    layers.tree_seconds()  # warm-up
+    first = layers.tree_seconds()
+    samples = [first]
+    if first[1] + first[2] < budget_s / 3:
+        samples += [layers.tree_seconds() for _ in range(2)]
+    per_tree = statistics.median(s[0] for s in samples)
+    return dict(tokens=layers.tokens, seconds_per_tree=per_tree, sliding_s=statistics.median(s[1] for s in samples),
+                global_s=statistics.median(s[2] for s in samples), runs=len(samples), cores=os.cpu_count(),
+                cpu=_cpu_model())
 
 
 def _cpu_model():
@@ -157,16 +166,18 @@ def _cpu_model():
 
 
 def reference_arm(args, rank, world):
+    """The reference arm: rank 0 times the CPU restatement of the reference lean path (no other rank works)."""
     if rank != 0:
         return
-    steps, vals = [], []
+    layers = CpuLayers()
+    steps = []
     for i in range(args.warmup + args.steps):
-        r = cpu_layer_baseline(60, budget_s=20.0)
+        per_tree, t_s, t_g = layers.tree_seconds()
         if i >= args.warmup:
-            steps.append(r)
-            vals.append(r['tokens'] / r['seconds_per_tree'])
+            steps.append(dict(tokens=layers.tokens, seconds_per_tree=per_tree, cores=os.cpu_count(),
+                              cpu=_cpu_model()))
     r = steps[-1]
-    value = r['tokens'] * len(vals) / sum(s['seconds_per_tree'] for s in steps)
+    value = r['tokens'] * len(steps) / sum(x['seconds_per_tree'] for x in steps)
     line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
                 ms_per_step=1000 * r['seconds_per_tree'], higher_is_better=True, scaling='weak', vs_baseline=None,
                 dtype='bf16', data='synthetic', impl='reference',
@@ -180,6 +191,66 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def kernel_arm(args):
+    """One kernel alone on a mid-size case (per-kernel timing and small ncu captures):
+    gemm / geglu: the 31B gate-up GEMM shape (M = 2040 text-tree tokens, K = 5376) with a plain or GeGLU epilogue;
+    attention / attention-window: the op-level paged tree attention (2048 + 8 x 64 tokens, 32/16 heads of 128, pages
+    of 64 through a shuffled page table), global or sliding window 1024."""
+    import torch
+    from morj_b200 import _native as nat
+    sys.path.insert(0, os.path.join(ROOT, 'tests'))
+    dev = torch.device('cuda', 0)
+    s = torch.cuda.current_stream().cuda_stream
+    if args.kernel in ('gemm', 'geglu'):
+        M, N, K = args.m, args.n, args.k
+        a = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        b = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+        epi = nat.EPI_GEGLU if args.kernel == 'geglu' else nat.EPI_STORE
+        c = torch.empty(M, N // 2 if epi else N, device=dev, dtype=torch.bfloat16)
+        flops = 2 * M * N * K
+
+        def launch():
+            nat.call('morj_gemm_bf16', a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), c.stride(0), M, N, K, epi, s)
+        shape = dict(M=M, N=N, K=K)
+    else:
+        from attn_cases import op_level_case, unmasked_pairs
+        window = 1024 if args.kernel == 'attention-window' else 0
+        case = op_level_case()
+        q, kp, vp = case['q'].to(dev), case['k_pool'].to(dev), case['v_pool'].to(dev)
+        out = torch.empty_like(q)
+        qo = case['qo_indptr']
+        work = np.zeros(2 * 4096, np.int32)
+        nw = nat.lib().morj_tree_attention_work(np.ascontiguousarray(qo).ctypes.data_as(nat.IP), len(qo) - 1,
+                                                case['hq'], case['hk'], work.ctypes.data_as(nat.IP), 4096)
+        t = [torch.as_tensor(x, device=dev) for x in (qo, case['kv_indptr'], case['kv_indices'],
+                                                       case['last_page_len'], work[:2 * nw])]
+        kv_len = [(case['kv_indptr'][i + 1] - case['kv_indptr'][i] - 1) * case['page_size'] + case['last_page_len'][i]
+                  for i in range(len(qo) - 1)]
+        flops = 4 * case['hq'] * case['d'] * unmasked_pairs(qo, kv_len, window)
+
+        def launch():
+            nat.call('morj_tree_attention', q.data_ptr(), kp.data_ptr(), vp.data_ptr(), out.data_ptr(), t[0].data_ptr(),
+                     t[1].data_ptr(), t[2].data_ptr(), t[3].data_ptr(), len(qo) - 1, 0, case['hq'], case['hk'],
+                     case['d'], case['page_size'], window, float(case['sm_scale']), t[4].data_ptr(), nw, s)
+        shape = dict(tokens=int(qo[-1]), window=window, pages=len(case['kv_indices']))
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    pk = peaks()
+    tf = flops / (ms / 1000) / 1e12
+    print(json.dumps(dict(kernel=args.kernel, shape=shape, ms=round(ms, 4), tflops=round(tf, 1),
+                          frac_of_burst_peak=round(tf / pk['bf16'], 4), peak_source=pk['source'],
+                          gflop=round(flops / 1e9, 2))), flush=True)
+    assert nat.device_error(s) == 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -188,7 +259,14 @@ def main():
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--kernel', choices=['gemm', 'geglu', 'attention', 'attention-window'],
+                    help='time one kernel alone instead of the tree forward')
+    ap.add_argument('--m', type=int, default=2040)
+    ap.add_argument('--n', type=int, default=43008)
+    ap.add_argument('--k', type=int, default=5376)
     args = ap.parse_args()
+    if args.kernel:
+        return kernel_arm(args)
     rank = int(os.environ.get('RANK', 0))
     world = int(os.environ.get('WORLD_SIZE', 1))
     if args.impl == 'reference':
@@ -294,7 +372,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            r = cpu_layer_baseline(60)
+            r = cpu_layer_baseline()
             cpu = dict(value=r['tokens'] / r['seconds_per_tree'], unit=UNIT, cores=r['cores'], kind='port',
                        sample=(f"one sliding ({r['sliding_s']:.2f} s) + one global ({r['global_s']:.2f} s) decoder "
                                f"layer at the full {r['tokens']}-token tree through oracle/lean_oracle.py (BF16, torch "

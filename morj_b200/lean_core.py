@@ -545,8 +545,8 @@ class LeanGemma4:
         M, K = a.shape
         N = w.shape[0] if w_rows is None else w_rows
         wp = w.data_ptr() + w_offset_rows * w.stride(0) * w.element_size()
-        self._k('gemm', 'morj_gemm_bf16', a.data_ptr(), a.stride(0), wp, w.stride(0), out.data_ptr(), out.stride(0),
-                M, N, K, epi, self._stream(), flops=2 * M * N * K)
+        self._k('gemm_geglu' if epi == nat.EPI_GEGLU else 'gemm', 'morj_gemm_bf16', a.data_ptr(), a.stride(0), wp,
+                w.stride(0), out.data_ptr(), out.stride(0), M, N, K, epi, self._stream(), flops=2 * M * N * K)
 
     def _attention(self, q, k_pool, v_pool, out, t, qo, kv_indptr, kv_indices, n_seg, n_bidir, kind, work, n_work):
         hk, d = self.geom[kind]

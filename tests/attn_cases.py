@@ -44,8 +44,8 @@ def unmasked_pairs(qo, kv_len, window):
     count is 4 * hq * d per pair."""
     total = 0
     for s in range(len(qo) - 1):
-        ql = qo[s + 1] - qo[s]
-        kl = kv_len[s]
+        ql = int(qo[s + 1]) - int(qo[s])
+        kl = int(kv_len[s])
         for j in range(ql):
             hi = kl - ql + j
             lo = max(0, hi - window + 1) if window > 0 else 0

@@ -1,17 +1,16 @@
 // Tree-masked paged prefill attention for sm_100a.
 //
-// One CTA (4 warps) handles one work tile: a segment's block of 128/G consecutive queries for one KV head, with the
-// G = hq/hk query heads that share that KV head packed into the 128 MMA rows (row = query * G + head). For every
-// chunk of 64 keys of the segment's key list it
-//   1. gathers the K and V rows of the chunk from the paged pool (slot = page * page_size + offset) into 128-byte-
-//      swizzled shared memory with cp.async (double-buffered: the next chunk loads while this one computes),
-//   2. issues S = Q K^T on the tensor cores (tcgen05.mma, M=128, N=64, accumulator in TMEM),
-//   3. reads S back (thread = row), applies the tree mask (bottom-right causal, sliding window, bidirectional image
-//      blocks) and the online softmax in FP32, and writes P as BF16 to shared memory,
-//   4. issues O_chunk = P V (tcgen05.mma with V as an N-major operand, so K and V share one shared-memory layout),
-//   5. accumulates O_chunk into registers with the softmax rescale.
-// The key range of a tile is cut to what its queries can see (the window and causal bounds), so a sliding layer's
-// long prefix costs O(window) per tile.
+// One CTA handles one work tile: a segment's block of 128/G consecutive queries for one KV head, the G = hq/hk query
+// heads that share that KV head packed into the 128 MMA rows (row = query * G + head). The CTA is warp-specialised:
+//   warp 0      loader: gathers the K and V rows of each 64-key chunk from the paged pool (slot = page * page_size +
+//               offset) into 128-byte-swizzled shared memory with cp.async, two chunks in flight
+//   warp 1      MMA issuer (one thread): S_c = Q K_c^T into one of two TMEM score buffers, then O += P_{c-1} V_{c-1}
+//               into the TMEM output, so the tensor cores compute chunk c+1's scores while the softmax works on c
+//   warps 2-5   softmax (thread = row): tree mask (bottom-right causal bound, sliding window, image-block rule), online
+//               softmax in FP32 with a lazily rescaled running maximum (O in TMEM is rescaled only when a row's
+//               maximum grows by more than 2^8), P as BF16 to shared memory, and the final O / l store
+// V is read as an N-major operand, so one shared-memory layout serves K (for QK^T) and V (for PV). The key range of a
+// tile is cut to what its queries can see, so a sliding layer's long prefix costs O(window) per tile.
 #include "common.cuh"
 
 namespace morj {
@@ -19,9 +18,10 @@ namespace attn {
 
 constexpr int ROWS = 128;
 constexpr int BN = 64;
-constexpr int THREADS = 128;
-constexpr int TMEM_COLS = 256;  // S at columns [0, 64), O chunk at [128, 128 + D)
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 256;  // S buffers at columns [0, 64) and [64, 128), O at [128, 128 + D)
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_LOG2 = 8.0f;  // rescale O only when a row maximum grows by more than 2^8
 
 template <int D>
 struct Smem {
@@ -33,8 +33,9 @@ struct Smem {
   static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;  // 2 buffers
   static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
   static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  // barriers; the dynamic shared window starts 1024-byte aligned (checked in the kernel), so two CTAs fit an SM
-  static constexpr int TOTAL = BAR_OFF + 64;
+  // barriers: kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full, o_done, done; then the TMEM slot and abort flag.
+  // The dynamic shared window starts 1024-byte aligned (checked in the kernel), so two CTAs fit an SM.
+  static constexpr int TOTAL = BAR_OFF + 128;
 };
 
 MORJ_DEV void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
@@ -57,20 +58,30 @@ MORJ_DEV int key_slot(const int* __restrict__ kv_indices, int kv_base, int t, in
   return page * page_size + t % page_size;
 }
 
-// gather K and V rows of keys [t0, t0 + BN) (zeros past t_end) into one buffer pair
+// warp-level wait: lane 0 polls the barrier, the warp follows its verdict
+MORJ_DEV bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  int ok = (threadIdx.x & 31) == 0 ? (int)mbar_wait(bar, parity, abort, kErrTimeoutAttention) : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// one warp gathers the K and V rows of keys [t0, t0 + BN) (zeros past t_end) into one buffer pair
 template <int D>
 MORJ_DEV void load_kv_chunk(uint32_t k_dst, uint32_t v_dst, const __nv_bfloat16* __restrict__ k_pool,
                             const __nv_bfloat16* __restrict__ v_pool, const int* __restrict__ kv_indices,
-                            const Segment& sg, int t0, int t_end, int hk, int h, int page_size) {
+                            const Segment& sg, int t0, int t_end, int hk, int h, int page_size, int lane) {
   constexpr int CH = D / 8;  // 16-byte chunks per row
-  for (int id = threadIdx.x; id < BN * CH; id += THREADS) {
-    const int k = id / CH, c16 = id % CH;
+  for (int k = lane; k < BN; k += 32) {
     const int t = t0 + k;
     const bool ok = t < t_end;
     const size_t row = ok ? ((size_t)key_slot(kv_indices, sg.kv_base, t, page_size) * hk + h) * D : 0;
-    const uint32_t off = (uint32_t)((c16 >> 3) * (BN * 128)) + sw128_offset(k, c16 & 7);
-    cp_async16(k_dst + off, k_pool + row + c16 * 8, ok ? 16u : 0u);
-    cp_async16(v_dst + off, v_pool + row + c16 * 8, ok ? 16u : 0u);
+    const __nv_bfloat16* ks = k_pool + row;
+    const __nv_bfloat16* vs = v_pool + row;
+#pragma unroll
+    for (int c16 = 0; c16 < CH; ++c16) {
+      const uint32_t off = (uint32_t)((c16 >> 3) * (BN * 128)) + sw128_offset(k, c16 & 7);
+      cp_async16(k_dst + off, ks + c16 * 8, ok ? 16u : 0u);
+      cp_async16(v_dst + off, vs + c16 * 8, ok ? 16u : 0u);
+    }
   }
 }
 
@@ -88,9 +99,11 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (threadIdx.x == 0) report(kErrBadAlignment);
     return;
   }
-  const uint32_t bar_s = sbase + L::BAR_OFF, bar_o = bar_s + 8, bar_d = bar_s + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 24);
-  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 28);
+  const uint32_t bar0 = sbase + L::BAR_OFF;
+  const uint32_t kv_full = bar0, kv_empty = bar0 + 16, s_full = bar0 + 32, s_free = bar0 + 48;
+  const uint32_t p_full = bar0 + 64, o_done = bar0 + 72, done = bar0 + 80;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 96);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 100);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int seg = work[2 * blockIdx.x], q0 = work[2 * blockIdx.x + 1];
@@ -121,21 +134,32 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int n_chunks = (t_end - t_begin + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_s, 1);
-    mbar_init(bar_o, 1);
-    mbar_init(bar_d, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(kv_full + 8 * b, 1);
+      mbar_init(kv_empty + 8 * b, 1);
+      mbar_init(s_full + 8 * b, 1);
+      mbar_init(s_free + 8 * b, 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_init(done, 1);
     *abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
     tmem_relinquish();
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  // Q tile: row r = query (r / G) of the tile, head h * G + r % G; zeros past the segment
-  {
+  if (warp == 0) {
+    // ---------------- loader ----------------
+    // chunk c goes to buffer c & 1; chunk 0's copy group also carries the Q tile
     constexpr int CH = D / 8;
-    for (int id = threadIdx.x; id < ROWS * CH; id += THREADS) {
+    for (int id = lane; id < ROWS * CH; id += 32) {
       const int r = id / CH, c16 = id % CH;
       const int qi = q0 + r / G;
       const bool ok = qi < sg.q_len;
@@ -143,169 +167,198 @@ __global__ void __launch_bounds__(THREADS, 2)
       const uint32_t off = (uint32_t)((c16 >> 3) * (ROWS * 128)) + sw128_offset(r, c16 & 7);
       cp_async16(sbase + L::Q_OFF + off, q + src + c16 * 8, ok ? 16u : 0u);
     }
-  }
-  load_kv_chunk<D>(sbase + L::K_OFF, sbase + L::V_OFF, k_pool, v_pool, kv_indices, sg, t_begin, t_end, hk, h,
-                   page_size);
-  cp_async_commit();
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
-  const uint32_t tm_s = t_lane, tm_o = t_lane + 128;  // this warp's lanes of S and O
-
-  // this thread's row
-  const int r = threadIdx.x;
-  const int qi = q0 + r / G;
-  const bool row_ok = qi < sg.q_len;
-  int lo, hi;  // visible key positions [lo, hi]
-  if (bidir) {
-    hi = sg.kv_len - 1;
-    lo = window > 0 ? diag + min(0, qi - (window - 1)) : 0;
-  } else {
-    hi = diag + qi;
-    lo = window > 0 ? hi - (window - 1) : 0;
-  }
-  if (!row_ok) {
-    lo = 1;
-    hi = 0;
-  }
-
-  float o_acc[D];
-#pragma unroll
-  for (int i = 0; i < D; ++i) o_acc[i] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
-
-  constexpr uint32_t IDESC_S = idesc_bf16(ROWS, BN);
-  constexpr uint32_t IDESC_O = idesc_bf16(ROWS, D, /*b_mn_major=*/true);
-  bool failed = false;
-
-  for (int ci = 0; ci < n_chunks; ++ci) {
-    const int buf = ci & 1;
-    const int t0 = t_begin + ci * BN;
-    if (ci + 1 < n_chunks) {
-      const int nb = buf ^ 1;
-      load_kv_chunk<D>(sbase + L::K_OFF + nb * L::KV_BYTES, sbase + L::V_OFF + nb * L::KV_BYTES, k_pool, v_pool,
-                       kv_indices, sg, t0 + BN, t_end, hk, h, page_size);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
+    // Chunk c is published (kv_full) as soon as it has landed, before the loader waits for a buffer to reuse: the
+    // issuer needs chunk c's keys to run S_c and then PV_{c-1}, and that PV is what frees the buffer of chunk c + 1.
+    load_kv_chunk<D>(sbase + L::K_OFF, sbase + L::V_OFF, k_pool, v_pool, kv_indices, sg, t_begin, t_end, hk, h,
+                     page_size, lane);
+    cp_async_commit();
+    bool ok = true;
+    for (int c = 1; c < n_chunks; ++c) {
       cp_async_wait<0>();
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-
-    const uint32_t k_s = sbase + L::K_OFF + buf * L::KV_BYTES;
-    const uint32_t v_s = sbase + L::V_OFF + buf * L::KV_BYTES;
-    if (threadIdx.x == 0) {
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t qa = sbase + L::Q_OFF + (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
-        const uint32_t kb = k_s + (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-        umma_bf16(tmem, sw128_desc(qa), sw128_desc(kb), IDESC_S, kk > 0);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(kv_full + 8 * ((c - 1) & 1));
+      const int b = c & 1;
+      if (c >= 2 && !warp_wait(kv_empty + 8 * b, ((c >> 1) - 1) & 1, abort)) {
+        ok = false;
+        break;
       }
-      umma_commit(bar_s);
+      load_kv_chunk<D>(sbase + L::K_OFF + b * L::KV_BYTES, sbase + L::V_OFF + b * L::KV_BYTES, k_pool, v_pool,
+                       kv_indices, sg, t_begin + c * BN, t_end, hk, h, page_size, lane);
+      cp_async_commit();
     }
-    // every warp's lane 0 waits; the CTA acts on one verdict so no thread is left at a barrier alone
-    int ok = lane == 0 ? (int)mbar_wait(bar_s, ci & 1, abort, kErrTimeoutAttention) : 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) {
-      failed = true;
-      break;
+    cp_async_wait<0>();
+    if (ok) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(kv_full + 8 * ((n_chunks - 1) & 1));
     }
-    tc_fence_after();
-
-    // scores of this row for keys t0 .. t0 + 63
-    uint32_t sr[2][32];
-    tmem_ld32(tm_s, sr[0]);
-    tmem_ld32(tm_s + 32, sr[1]);
-    tmem_wait_ld();
-    float s[BN];
-    float mx = -INFINITY;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(ROWS, BN);
+      constexpr uint32_t IDESC_O = idesc_bf16(ROWS, D, /*b_mn_major=*/true);
+      bool ok = true;
+      auto issue_pv = [&](int j) -> bool {
+        if (!mbar_wait(p_full, j & 1, abort, kErrTimeoutAttention)) return false;
+        tc_fence_after();
+        const uint32_t v_s = sbase + L::V_OFF + (j & 1) * L::KV_BYTES;
 #pragma unroll
-    for (int j = 0; j < BN; ++j) {
-      const int t = t0 + j;
-      const bool vis = t >= lo && t <= hi;
-      s[j] = vis ? __uint_as_float(sr[j >> 5][j & 31]) * scale_log2 : -INFINITY;
-      mx = fmaxf(mx, s[j]);
-    }
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
-    float psum = 0.f;
-    uint32_t pk[BN / 2];
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t pa = sbase + L::P_OFF + kk * 32;
+          const uint32_t vb = v_s + kk * 2048;
+          umma_bf16(tmem + 128, sw128_desc(pa), sw128_desc(vb, BN * 128), IDESC_O, (j | kk) != 0);
+        }
+        umma_commit(o_done);
+        umma_commit(kv_empty + 8 * (j & 1));
+        return true;
+      };
+      for (int c = 0; c < n_chunks && ok; ++c) {
+        const int b = c & 1;
+        if (!mbar_wait(kv_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention)) {
+          ok = false;
+          break;
+        }
+        if (c >= 2 && !mbar_wait(s_free + 8 * b, ((c >> 1) - 1) & 1, abort, kErrTimeoutAttention)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_s = sbase + L::K_OFF + b * L::KV_BYTES;
 #pragma unroll
-    for (int j = 0; j < BN; j += 2) {
-      const float p0 = (s[j] == -INFINITY) ? 0.f : exp2f(s[j] - m_new);
-      const float p1 = (s[j + 1] == -INFINITY) ? 0.f : exp2f(s[j + 1] - m_new);
-      psum += p0 + p1;
-      pk[j / 2] = pack_bf16x2(p0, p1);
-    }
-    l_run = l_run * alpha + psum;
-    m_run = m_new;
-    // P row r -> shared memory (K-major, one 128-byte swizzle atom wide)
-    {
-      uint8_t* prow = smem + L::P_OFF;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4*>(prow + sw128_offset(r, c)) = v;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t qa = sbase + L::Q_OFF + (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
+          const uint32_t kb = k_s + (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          umma_bf16(tmem + b * BN, sw128_desc(qa), sw128_desc(kb), IDESC_S, kk > 0);
+        }
+        umma_commit(s_full + 8 * b);
+        if (c >= 1) ok = issue_pv(c - 1);
       }
+      if (ok) issue_pv(n_chunks - 1);
+      // TMEM is freed only after every MMA issued here has completed
+      umma_commit(done);
+      mbar_wait_landed(done, 0);
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (threadIdx.x == 0) {
-#pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk) {
-        const uint32_t pa = sbase + L::P_OFF + kk * 32;
-        const uint32_t vb = v_s + kk * 2048;
-        umma_bf16(tmem + 128, sw128_desc(pa), sw128_desc(vb, BN * 128), IDESC_O, kk > 0);
+  } else {
+    // ---------------- softmax warpgroup ----------------
+    const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. + 31
+    const int r = quarter * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int qi = q0 + r / G;
+    const bool row_ok = qi < sg.q_len;
+    int lo, hi;  // visible key positions [lo, hi]
+    if (bidir) {
+      hi = sg.kv_len - 1;
+      lo = window > 0 ? diag + min(0, qi - (window - 1)) : 0;
+    } else {
+      hi = diag + qi;
+      lo = window > 0 ? hi - (window - 1) : 0;
+    }
+    if (!row_ok) {
+      lo = 1;
+      hi = 0;
+    }
+    float m_used = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    uint8_t* prow = smem + L::P_OFF;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int b = c & 1;
+      if (!warp_wait(s_full + 8 * b, (c >> 1) & 1, abort)) {
+        ok = false;
+        break;
       }
-      umma_commit(bar_o);
-    }
-    ok = lane == 0 ? (int)mbar_wait(bar_o, ci & 1, abort, kErrTimeoutAttention) : 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) {
-      failed = true;
-      break;
-    }
-    tc_fence_after();
-#pragma unroll
-    for (int c = 0; c < D; c += 32) {
-      uint32_t orr[32];
-      tmem_ld32(tm_o + c, orr);
+      tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32(t_lane + b * BN, sr[0]);
+      tmem_ld32(t_lane + b * BN + 32, sr[1]);
       tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free + 8 * b);
+      const int t0 = t_begin + c * BN;
+      float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) o_acc[c + i] = o_acc[c + i] * alpha + __uint_as_float(orr[i]);
+      for (int j = 0; j < BN; ++j) {
+        const int t = t0 + j;
+        const float v = (t >= lo && t <= hi) ? __uint_as_float(sr[j >> 5][j & 31]) * scale_log2 : -INFINITY;
+        sr[j >> 5][j & 31] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      float alpha = 1.f;
+      if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
+        if (m_used != -INFINITY) alpha = fast_exp2(m_used - mx);
+        if (mx != -INFINITY) m_used = mx;
+      }
+      l_run *= alpha;
+      float psum = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int j = 0; j < BN; j += 2) {
+        const float s0 = __uint_as_float(sr[j >> 5][j & 31]);
+        const float s1 = __uint_as_float(sr[(j + 1) >> 5][(j + 1) & 31]);
+        const float p0 = s0 == -INFINITY ? 0.f : fast_exp2(s0 - m_used);
+        const float p1 = s1 == -INFINITY ? 0.f : fast_exp2(s1 - m_used);
+        psum += p0 + p1;
+        pk[j / 2] = pack_bf16x2(p0, p1);
+      }
+      l_run += psum;
+      // P and O are free once the previous chunk's PV has completed
+      if (c >= 1) {
+        if (!warp_wait(o_done, (c - 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int col = 0; col < D; col += 32) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + 128 + col, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_lane + 128 + col, o);
+          }
+          tmem_wait_st();
+        }
+      }
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint4 v = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+        *reinterpret_cast<uint4*>(prow + sw128_offset(r, cc)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && warp_wait(o_done, (n_chunks - 1) & 1, abort)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* dst = out + ((size_t)(sg.q_start + qi) * hq + h * G + r % G) * D;
+#pragma unroll 1
+      for (int col = 0; col < D; col += 32) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + 128 + col, o);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[v8 * 8 + 0]) * inv, __uint_as_float(o[v8 * 8 + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(o[v8 * 8 + 2]) * inv, __uint_as_float(o[v8 * 8 + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(o[v8 * 8 + 4]) * inv, __uint_as_float(o[v8 * 8 + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(o[v8 * 8 + 6]) * inv, __uint_as_float(o[v8 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + col + v8 * 8) = v;
+          }
+        }
+      }
     }
   }
 
-  if (!failed && row_ok) {
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    __nv_bfloat16* dst = out + ((size_t)(sg.q_start + qi) * hq + h * G + r % G) * D;
-#pragma unroll
-    for (int c = 0; c < D; c += 8) {
-      uint4 v;
-      v.x = pack_bf16x2(o_acc[c + 0] * inv, o_acc[c + 1] * inv);
-      v.y = pack_bf16x2(o_acc[c + 2] * inv, o_acc[c + 3] * inv);
-      v.z = pack_bf16x2(o_acc[c + 4] * inv, o_acc[c + 5] * inv);
-      v.w = pack_bf16x2(o_acc[c + 6] * inv, o_acc[c + 7] * inv);
-      *reinterpret_cast<uint4*>(dst + c) = v;
-    }
-  }
-  // exit: no copy or MMA of this CTA may be in flight when its shared memory and TMEM go away
-  cp_async_wait<0>();
-  if (failed && threadIdx.x == 0) {
-    umma_commit(bar_d);
-    mbar_wait_landed(bar_d, 0);
-  }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }

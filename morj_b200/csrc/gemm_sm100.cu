@@ -1,11 +1,12 @@
 // BF16 projection GEMM for sm_100a: C = A . B^T with FP32 accumulation in TMEM.
 //
 // Persistent, warp-specialised kernel, one CTA per SM:
-//   warp 0      TMA producer: A [128 x 64] and B [256 x 64] tiles (128-byte swizzle) into a 4-stage ring
-//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator, commits each
+//   warp 0      TMA producer: A [128 x 64] and B [BN x 64] tiles (128-byte swizzle) into a 4-6 stage ring
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator, commits each
 //               stage back to the producer and each finished tile to the epilogue
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (thread = row), BF16 rounding and the fused epilogue
-// Two 256-column accumulators (all 512 TMEM columns) let the epilogue of tile i overlap the main loop of i+1.
+// Two accumulators (all 512 TMEM columns) let the epilogue of tile i overlap the main loop of i+1. The tile width
+// BN (128..256) is chosen per shape so the tile count fills whole waves of the 148 SMs.
 // Tiles are walked in groups of 16 row-blocks so the activation slice and the weight tiles of the CTAs in flight
 // stay in L2. No TMA multicast is used, so the kernel is valid whichever GPU's memory the pointers refer to.
 #include <mutex>
@@ -15,15 +16,23 @@
 namespace morj {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 512;
+constexpr int TMEM_COLS = 512;  // two accumulators, at columns 0 and 256
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+
+// Tile width BN (a multiple of 16, at most 256): the host picks it per shape so the tile count fills whole waves of
+// the SMs; the stage ring is as deep as shared memory allows.
+template <int BN>
+struct Cfg {
+  static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "tile width");
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (220 * 1024) / STAGE_BYTES > 6 ? 6 : (220 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+};
 
 struct TileCoord {
   int m, n;
@@ -38,21 +47,22 @@ MORJ_DEV TileCoord tile_coord(int t, int num_m, int num_n) {
   return {first_m + local % gm, local / gm};
 }
 
-template <int EPI>
+template <int EPI, int BN>
 MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv_bfloat16* C, long long ldc, int N) {
   if constexpr (EPI == MORJ_EPI_STORE) {
     __nv_bfloat16* crow = C + (size_t)row * ldc;
+    const int lim = min(N, (n_blk + 1) * BN);  // this tile's columns (the last 32-column load may run past BN)
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       uint32_t r[32];
       tmem_ld32(tacc + c, r);
       tmem_wait_ld();
       const int col = n_blk * BN + c;
-      if (row_ok && col < N) {
+      if (row_ok && col < lim) {
         uint4* dst = reinterpret_cast<uint4*>(crow + col);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
-          if (col + v * 8 < N) {
+          if (col + v * 8 < lim) {
             uint4 pk;
             pk.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
             pk.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
@@ -97,10 +107,12 @@ MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv
   }
 }
 
-template <int EPI>
+template <int EPI, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K) {
+  using C_ = Cfg<BN>;
+  constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -185,7 +197,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
         if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kErrTimeoutGemmMma)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * 256;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(full0 + 8 * stage, phase, abort, kErrTimeoutGemmMma)) {
@@ -197,7 +209,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_bf16(d_tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), IDESC, (kb | k) != 0);
+            umma_bf16(d_tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), C_::IDESC, (kb | k) != 0);
           }
           umma_commit(empty0 + 8 * stage);
           if (++stage == STAGES) {
@@ -229,8 +241,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       const int row = tc.m * BM + quarter * 32 + lane;
-      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      epilogue_tile<EPI>(tacc, row, tc.n, row < M, C, ldc, N);
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
+      epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
       tc_fence_before();
       mbar_arrive(acce0 + 8 * acc);
       if (++acc == 2) {
@@ -294,12 +306,14 @@ static int num_sms() {
   return n;
 }
 
-template <int EPI>
+template <int EPI, int BN>
 static int launch(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
                   int K, cudaStream_t stream) {
+  using C_ = Cfg<BN>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C_::SMEM_BYTES);
     if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = true;
   }
@@ -310,8 +324,27 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
   if (st) return st;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K);
+  gemm_kernel<EPI, BN><<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc,
+                                                                   M, N, K);
   return check_launch("gemm_kernel");
+}
+
+// Tile width for a plain GEMM: the smallest (waves x (BN + 16)), where a wave is one tile per SM and the 16 stands for
+// the per-tile cost that does not shrink with BN; ties go to the wider tile.
+static int pick_bn(int M, int N) {
+  static const int cand[] = {256, 240, 224, 208, 192, 176, 160, 128};
+  const int sms = num_sms();
+  int best = 256;
+  long long best_cost = -1;
+  for (int bn : cand) {
+    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    const long long cost = ((tiles + sms - 1) / sms) * (bn + 16);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 }  // namespace gemm
@@ -330,12 +363,21 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (epilogue == MORJ_EPI_STORE) {
     if (N % 16 || ldc < N) return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: N must be a multiple of 16 (N=%d)", N);
-    return gemm::launch<MORJ_EPI_STORE>(A, lda, B, ldb, C, ldc, M, N, K, s);
+    switch (gemm::pick_bn(M, N)) {
+      case 240: return gemm::launch<MORJ_EPI_STORE, 240>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      case 224: return gemm::launch<MORJ_EPI_STORE, 224>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      case 208: return gemm::launch<MORJ_EPI_STORE, 208>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      case 192: return gemm::launch<MORJ_EPI_STORE, 192>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      case 176: return gemm::launch<MORJ_EPI_STORE, 176>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      case 160: return gemm::launch<MORJ_EPI_STORE, 160>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      case 128: return gemm::launch<MORJ_EPI_STORE, 128>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      default: return gemm::launch<MORJ_EPI_STORE, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
+    }
   }
   if (epilogue == MORJ_EPI_GEGLU) {
-    if (N % gemm::BN || ldc < N / 2)
+    if (N % 256 || ldc < N / 2)
       return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: GEGLU needs N a multiple of 256 (N=%d)", N);
-    return gemm::launch<MORJ_EPI_GEGLU>(A, lda, B, ldb, C, ldc, M, N, K, s);
+    return gemm::launch<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
   }
   return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: unknown epilogue %d", epilogue);
 }

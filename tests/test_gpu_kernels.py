@@ -47,7 +47,10 @@ def _device():
 
 
 @pytest.mark.parametrize('M,N,K', [(1, 16, 64), (37, 272, 200), (128, 256, 64), (300, 512, 1024),
-                                   (2040, 768, 5376), (517, 5376, 4096), (9, 4096, 5376)])
+                                   (2040, 768, 5376), (517, 5376, 4096), (9, 4096, 5376),
+                                   # the 31B shapes: each picks a different tile width (208, 224, 240, 128 / 192)
+                                   (2040, 5376, 4096), (2040, 8192, 576), (2040, 6144, 512), (9, 5376, 2048),
+                                   (5116, 4096, 256), (8704, 2048, 128)])
 def test_gemm_store_matches_fp32_matmul(M, N, K):
     g = torch.Generator(device=DEV).manual_seed(M * 7 + N)
     a = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)

@@ -201,7 +201,27 @@ def kernel_arm(args):
     sys.path.insert(0, os.path.join(ROOT, 'tests'))
     dev = torch.device('cuda', 0)
     s = torch.cuda.current_stream().cuda_stream
-    if args.kernel in ('gemm', 'geglu'):
+    if args.kernel == 'qkv':
+        # the sliding-layer QKV projection with the fused head norm + RoPE + pool scatter epilogue
+        M, H, d, hq, hk = args.m, 5376, 128, 32, 16
+        n_out = (hq + 2 * hk) * d
+        a = torch.randn(M, H, device=dev).to(torch.bfloat16)
+        w = (torch.randn(n_out, H, device=dev) * 0.02).to(torch.bfloat16)
+        qn = torch.ones(d, device=dev, dtype=torch.bfloat16)
+        pos = torch.arange(M, device=dev, dtype=torch.int32)
+        inv = (1.0 / (10000 ** (torch.arange(0, d, 2, device=dev).float() / d))).contiguous()
+        slots = torch.randperm(M, device=dev).to(torch.int32)
+        q_out = torch.empty(M, hq, d, device=dev, dtype=torch.bfloat16)
+        kp = torch.empty(M, hk, d, device=dev, dtype=torch.bfloat16)
+        vp = torch.empty(M, hk, d, device=dev, dtype=torch.bfloat16)
+        flops = 2 * M * n_out * H
+
+        def launch():
+            nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, 1, d, qn.data_ptr(),
+                     qn.data_ptr(), pos.data_ptr(), inv.data_ptr(), slots.data_ptr(), 1e-6, q_out.data_ptr(),
+                     kp.data_ptr(), vp.data_ptr(), s)
+        shape = dict(M=M, N=n_out, K=H)
+    elif args.kernel in ('gemm', 'geglu'):
         M, N, K = args.m, args.n, args.k
         a = torch.randn(M, K, device=dev).to(torch.bfloat16)
         b = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
@@ -259,7 +279,7 @@ def main():
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--kernel', choices=['gemm', 'geglu', 'attention', 'attention-window'],
+    ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window'],
                     help='time one kernel alone instead of the tree forward')
     ap.add_argument('--m', type=int, default=2040)
     ap.add_argument('--n', type=int, default=43008)

@@ -9,6 +9,7 @@
  * Reference interfaces replaced (ALERIA-ML/MORJ, aleria_judge/lean_core.py):
  *   morj_gemm_bf16            torch.matmul (cuBLAS) at lean_core.py:670,682,685,686,701,708,729,733
  *   morj_gemm_bf16 (GEGLU)    the gate-up matmul + flashinfer.activation.gelu_tanh_and_mul, lean_core.py:685,733
+ *   morj_gemm_qkv_rope        the QKV matmul + Triton _qkv_post, lean_core.py:670-674, 701-704, 708-712
  *   morj_embed_rmsnorm        embedding gather * embed_scale + image feature rows + flashinfer.rmsnorm,
  *                             lean_core.py:641-653
  *   morj_qkv_post             Triton _qkv_post, lean_core.py:234-277 (launches 672-674, 702-704, 710-712) with the
@@ -41,6 +42,8 @@ extern "C" {
 #define MORJ_EPI_STORE 0 /* C[M,N] = bf16(A[M,K] . B[N,K]^T) */
 #define MORJ_EPI_GEGLU 1 /* B rows interleaved in 128-row blocks (gate block, up block, ...); C[M,N/2] =
                             bf16(gelu_tanh(bf16(gate)) * bf16(up)) */
+#define MORJ_EPI_QKV_D128 2 /* internal: the fused QKV epilogue of morj_gemm_qkv_rope, 128-wide heads */
+#define MORJ_EPI_QKV_D64 3  /* internal: the same, 64-wide heads */
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 int morj_version(void);
@@ -57,6 +60,17 @@ int morj_device_error(int* code, int clear, void* stream);
  * Requires K % 8 == 0, lda/ldb/ldc % 8 == 0, 16-byte aligned pointers, N % 16 == 0 (N % 256 == 0 for GEGLU). */
 int morj_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
                    int K, int epilogue, void* stream);
+
+/* The QKV projection with the head epilogue fused: [q | k | v] = A . W^T (W: [N, K] rows q heads, k heads, v heads if
+ * has_v; N = (hq + (1 + has_v) * hk) * d), each head RMSNorm'ed over the BF16-rounded projection (q, k weighted;
+ * v unweighted), rounded, RoPE'd (q, k) and written straight to q_out[row, hq, d] and pool row slots[row] of
+ * k_pool / v_pool. has_v = 0 (full-attention layers): V = the unweighted norm of the K projection. hq = 0 or hk = 0
+ * give the K/V-only and q-only calls. Equivalent to morj_gemm_bf16 followed by morj_qkv_post, without the
+ * intermediate [M, N] tensor. d in {64, 128}. */
+int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, long long ldw, int M, int K, int hq, int hk,
+                       int has_v, int d, const void* q_norm, const void* k_norm, const int* positions,
+                       const float* inv_freq, const int* slots, float eps, void* q_out, void* k_pool, void* v_pool,
+                       void* stream);
 
 /* Per row i < n: x[i] = bf16(embed[tokens[i]] * scale), or the feature row features[feature_row[i]] when
  * feature_row != NULL and feature_row[i] >= 0; then h[i] = bf16(rmsnorm(x[i]) * norm_w) (FP32 math). H % 8 == 0. */

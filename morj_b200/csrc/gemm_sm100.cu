@@ -38,6 +38,120 @@ struct TileCoord {
   int m, n;
 };
 
+// Operands of the fused QKV epilogue: per-head RMSNorm (q, k weighted; v unweighted) of the BF16-rounded projection,
+// BF16 rounding, rotate-half RoPE on q and k, and the scatter of q to its packed rows and of k / v to pool slots.
+struct QkvEpi {
+  int hq, hk, has_v;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const int* positions;
+  const float* inv_freq;
+  const int* slots;
+  float eps;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+};
+
+MORJ_DEV void store32_bf16(__nv_bfloat16* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 pk;
+    pk.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+    pk.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+    pk.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+    pk.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    reinterpret_cast<uint4*>(dst)[q] = pk;
+  }
+}
+
+// One 128-row tile of the QKV projection, D-wide heads: thread = token row (reference `_qkv_post` numerics).
+template <int BN, int D>
+MORJ_DEV void epilogue_qkv(uint32_t tacc, int row, int n_blk, bool row_ok, const QkvEpi& e, int N) {
+  constexpr int HALF = D / 2;
+  const int n_heads = N / D;
+  const float pos = row_ok ? (float)e.positions[row] : 0.f;
+  const size_t slot = (row_ok && e.hk) ? (size_t)e.slots[row] : 0;
+#pragma unroll 1
+  for (int hh = 0; hh < BN / D; ++hh) {
+    const int head = (n_blk * BN) / D + hh;
+    if (head >= n_heads) break;
+    const uint32_t tb = tacc + hh * D;
+    const bool is_q = head < e.hq;
+    const bool is_k = !is_q && head < e.hq + e.hk;
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tb + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float v = bf16_round(__uint_as_float(r[i]));
+        ss += v * v;
+      }
+    }
+    const float inv = 1.0f / sqrtf(ss / D + e.eps);
+    const __nv_bfloat16* w = is_q ? e.q_norm : e.k_norm;
+    __nv_bfloat16* dst;
+    __nv_bfloat16* dst_v = nullptr;  // full-attention layers: V is the unweighted norm of the K projection
+    if (is_q) {
+      dst = e.q_out + ((size_t)row * e.hq + head) * D;
+    } else if (is_k) {
+      dst = e.k_pool + (slot * e.hk + (head - e.hq)) * D;
+      if (!e.has_v) dst_v = e.v_pool + (slot * e.hk + (head - e.hq)) * D;
+    } else {
+      dst = e.v_pool + (slot * e.hk + (head - e.hq - e.hk)) * D;
+    }
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 32) {
+      uint32_t r1[32], r2[32];
+      tmem_ld32(tb + c, r1);
+      tmem_ld32(tb + HALF + c, r2);
+      tmem_wait_ld();
+      float o1[32], o2[32];
+      if (is_q || is_k) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = bf16_round(__uint_as_float(r1[i])) * inv;
+          const float b = bf16_round(__uint_as_float(r2[i])) * inv;
+          const float y1 = bf16_round(a * __bfloat162float(w[c + i]));  // rounded before RoPE, as the reference
+          const float y2 = bf16_round(b * __bfloat162float(w[HALF + c + i]));
+          float sn, cs;
+          sincosf(pos * e.inv_freq[c + i], &sn, &cs);
+          o1[i] = y1 * cs - y2 * sn;
+          o2[i] = y2 * cs + y1 * sn;
+        }
+        if (row_ok) {
+          store32_bf16(dst + c, o1);
+          store32_bf16(dst + HALF + c, o2);
+        }
+        if (dst_v != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            o1[i] = bf16_round(__uint_as_float(r1[i])) * inv;
+            o2[i] = bf16_round(__uint_as_float(r2[i])) * inv;
+          }
+          if (row_ok) {
+            store32_bf16(dst_v + c, o1);
+            store32_bf16(dst_v + HALF + c, o2);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o1[i] = bf16_round(__uint_as_float(r1[i])) * inv;
+          o2[i] = bf16_round(__uint_as_float(r2[i])) * inv;
+        }
+        if (row_ok) {
+          store32_bf16(dst + c, o1);
+          store32_bf16(dst + HALF + c, o2);
+        }
+      }
+    }
+  }
+}
+
 MORJ_DEV TileCoord tile_coord(int t, int num_m, int num_n) {
   const int per_group = GROUP_M * num_n;
   const int group = t / per_group;
@@ -110,7 +224,7 @@ MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv
 template <int EPI, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K) {
+                __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe) {
   using C_ = Cfg<BN>;
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
@@ -242,7 +356,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int row = tc.m * BM + quarter * 32 + lane;
       const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
-      epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
+      if constexpr (EPI == MORJ_EPI_QKV_D128) {
+        epilogue_qkv<BN, 128>(tacc, row, tc.n, row < M, qe, N);
+      } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
+        epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
+      } else {
+        epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
+      }
       tc_fence_before();
       mbar_arrive(acce0 + 8 * acc);
       if (++acc == 2) {
@@ -308,7 +428,7 @@ static int num_sms() {
 
 template <int EPI, int BN>
 static int launch(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
-                  int K, cudaStream_t stream) {
+                  int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}) {
   using C_ = Cfg<BN>;
   static bool configured = false;
   if (!configured) {
@@ -325,21 +445,28 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   gemm_kernel<EPI, BN><<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                                                   M, N, K);
+                                                                   M, N, K, qe);
   return check_launch("gemm_kernel");
 }
 
-// Tile width for a plain GEMM: the smallest (waves x (BN + 16)), where a wave is one tile per SM and the 16 stands for
-// the per-tile cost that does not shrink with BN; ties go to the wider tile.
-static int pick_bn(int M, int N) {
-  static const int cand[] = {256, 240, 224, 208, 192, 176, 160, 128};
+// Tile width: the smallest (waves x per-tile time) over the candidates, where a wave is one tile per SM and a tile's
+// time per 64-deep k-block is the larger of its MMA time (2 x BN cycles for M = 128) and the time to fill its A and B
+// stage from L2 (about 1.28 cycles per 128-byte row, 128 + BN rows); ties go to the wider tile.
+static int pick_bn(int M, int N, const int* cand = nullptr, int n_cand = 0) {
+  static const int all[] = {256, 240, 224, 208, 192, 176, 160, 128};
+  if (!cand) {
+    cand = all;
+    n_cand = 8;
+  }
   const int sms = num_sms();
-  int best = 256;
-  long long best_cost = -1;
-  for (int bn : cand) {
+  int best = cand[0];
+  double best_cost = -1;
+  for (int i = 0; i < n_cand; ++i) {
+    const int bn = cand[i];
     const long long tiles = (long long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-    const long long cost = ((tiles + sms - 1) / sms) * (bn + 16);
-    if (best_cost < 0 || cost < best_cost) {
+    const double per_tile = 2.0 * bn > 1.28 * (BM + bn) ? 2.0 * bn : 1.28 * (BM + bn);
+    const double cost = (double)((tiles + sms - 1) / sms) * per_tile;
+    if (best_cost < 0 || cost < best_cost - 1e-9) {
       best_cost = cost;
       best = bn;
     }
@@ -380,4 +507,35 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
     return gemm::launch<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
   }
   return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: unknown epilogue %d", epilogue);
+}
+
+extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, long long ldw, int M, int K, int hq,
+                                  int hk, int has_v, int d, const void* q_norm, const void* k_norm,
+                                  const int* positions, const float* inv_freq, const int* slots, float eps,
+                                  void* q_out, void* k_pool, void* v_pool, void* stream) {
+  using namespace morj;
+  if (M == 0 || hq + hk == 0) return MORJ_OK;
+  if (!A || !W || !positions || !inv_freq || M < 0 || K <= 0 || hq < 0 || hk < 0 || (hq && (!q_out || !q_norm)) ||
+      (hk && (!k_pool || !v_pool || !slots || !k_norm)))
+    return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: bad pointers or sizes");
+  if (K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: K and leading dimensions must be multiples of 8");
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) & 15)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: pointers must be 16-byte aligned");
+  const int N = (hq + (has_v ? 2 : 1) * hk) * d;
+  gemm::QkvEpi e{hq, hk, has_v ? 1 : 0, (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, positions,
+                 inv_freq, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool, (__nv_bfloat16*)v_pool};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  static const int cand[] = {256, 128};
+  if (d == 128) {
+    if (gemm::pick_bn(M, N, cand, 2) == 128)
+      return gemm::launch<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+    return gemm::launch<MORJ_EPI_QKV_D128, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+  }
+  if (d == 64) {
+    if (gemm::pick_bn(M, N, cand, 2) == 128)
+      return gemm::launch<MORJ_EPI_QKV_D64, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+    return gemm::launch<MORJ_EPI_QKV_D64, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+  }
+  return set_error(MORJ_ERR_UNSUPPORTED, "morj_gemm_qkv_rope: head_dim %d unsupported (64, 128)", d);
 }

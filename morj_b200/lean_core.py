@@ -9,7 +9,7 @@ operation of the forward is a hand-written sm_100a kernel reached through the C-
 no cuBLAS, FlashInfer or Triton, and no CPU fallback.
 
 Forward per step (one pass may need several steps; see `Tree.plan_pass`):
-  embed + input norm -> per layer: QKV GEMM -> head norm + RoPE + pool scatter -> tree attention -> O GEMM ->
+  embed + input norm -> per layer: QKV GEMM with head norm + RoPE + pool scatter fused -> tree attention -> O GEMM ->
   residual + norms -> gate/up GEMM with GeGLU epilogue -> down GEMM -> residual * scalar + next input norm;
   the last layer computes K/V for every token and the rest only for readout rows; the label head reads them.
 Numerics follow the reference path: FP32 norms and softmax, BF16 rounding where it rounds, attention scale 1.0,
@@ -548,6 +548,18 @@ class LeanGemma4:
         self._k('gemm_geglu' if epi == nat.EPI_GEGLU else 'gemm', 'morj_gemm_bf16', a.data_ptr(), a.stride(0), wp,
                 w.stride(0), out.data_ptr(), out.stride(0), M, N, K, epi, self._stream(), flops=2 * M * N * K)
 
+    def _qkv(self, a, layer, row0, M, hq, hk, has_v, d, kind, positions, slots, q_out, k_pool, v_pool):
+        """QKV projection with the fused head norm + RoPE + pool scatter (`morj_gemm_qkv_rope`); `row0` skips the q
+        rows of the fused weight for the K/V-only call."""
+        w = layer['qkv']
+        H = a.shape[1]
+        n_out = (hq + (2 if has_v else 1) * hk) * d
+        flops = 2 * M * n_out * H
+        wp = w.data_ptr() + row0 * w.stride(0) * w.element_size()
+        self._k('gemm_qkv', 'morj_gemm_qkv_rope', a.data_ptr(), a.stride(0), wp, w.stride(0), M, H, hq, hk, has_v,
+                d, layer['q_norm'].data_ptr(), layer['k_norm'].data_ptr(), positions, self.inv_freq[kind].data_ptr(),
+                slots, self.eps, _ptr(q_out), _ptr(k_pool), _ptr(v_pool), self._stream(), flops=flops)
+
     def _attention(self, q, k_pool, v_pool, out, t, qo, kv_indptr, kv_indices, n_seg, n_bidir, kind, work, n_work):
         hk, d = self.geom[kind]
         window = self.window if kind == 'sliding_attention' else 0
@@ -582,8 +594,6 @@ class LeanGemma4:
         attn = torch.empty(n, hq * d_max, dtype=bf, device=dev)
         o = torch.empty(n, H, dtype=bf, device=dev)
         act = torch.empty(n, F, dtype=bf, device=dev)
-        qkv_w = max(l['qkv'].shape[0] for l in self.layers)
-        qkv = torch.empty(n, qkv_w, dtype=bf, device=dev)
         for i, layer in enumerate(self.layers):
             kind = layer['kind']
             hk, d = self.geom[kind]
@@ -597,14 +607,9 @@ class LeanGemma4:
             has_v = int(kind == 'sliding_attention')
             if i == last and self.prune_last:
                 return self._last_layer(t, rows, n_work, layer, h, x, k_pool, v_pool, kind, has_v)
-            nq = layer['qkv'].shape[0]
-            qkv_i = qkv[:, :nq]
-            self._gemm(h, layer['qkv'], qkv_i)
             q_i = q[:, :hq * d]
-            self._k('rows', 'morj_qkv_post', qkv_i.data_ptr(), qkv.stride(0), n, hq, hk, has_v, d,
-                     layer['q_norm'].data_ptr(), layer['k_norm'].data_ptr(), t.ptr('positions'),
-                     self.inv_freq[kind].data_ptr(), t.ptr('slots_' + kk), eps, q_i.data_ptr(), k_pool.data_ptr(),
-                     v_pool.data_ptr(), s)
+            self._qkv(h, layer, 0, n, hq, hk, has_v, d, kind, t.ptr('positions'), t.ptr('slots_' + kk), q_i,
+                      k_pool, v_pool)
             a_i = attn[:, :hq * d]
             self._attention(q_i, k_pool, v_pool, a_i, t, 'qo', 'kv_indptr_' + kk, 'kv_indices_' + kk, n_seg,
                             nb if kind == 'sliding_attention' else 0, kind, 'work_' + kk, n_work[kk])
@@ -633,23 +638,16 @@ class LeanGemma4:
         kk = KINDS[kind]
         dev, bf = self.device, torch.bfloat16
         qd = hq * d
-        kvw = layer['qkv'].shape[0] - qd
-        kv = torch.empty(n, kvw, dtype=bf, device=dev)
-        self._gemm(h, layer['qkv'], kv, w_rows=kvw, w_offset_rows=qd)
-        self._k('rows', 'morj_qkv_post', kv.data_ptr(), kvw, n, 0, hk, has_v, d, layer['q_norm'].data_ptr(),
-                 layer['k_norm'].data_ptr(), t.ptr('positions'), self.inv_freq[kind].data_ptr(), t.ptr('slots_' + kk),
-                 eps, None, k_pool.data_ptr(), v_pool.data_ptr(), s)
+        # K/V of every token (later readouts attend to them), straight into the pools
+        self._qkv(h, layer, qd, n, 0, hk, has_v, d, kind, t.ptr('positions'), t.ptr('slots_' + kk), None, k_pool,
+                  v_pool)
         if not rows:
             return None, []
         R = len(rows)
         hr = torch.empty(R, H, dtype=bf, device=dev)
         self._k('rows', 'morj_gather_rows', h.data_ptr(), H, t.ptr('ro_rows'), R, H, hr.data_ptr(), H, s)
-        q_lin = torch.empty(R, qd, dtype=bf, device=dev)
-        self._gemm(hr, layer['qkv'], q_lin, w_rows=qd)
         q = torch.empty(R, qd, dtype=bf, device=dev)
-        self._k('rows', 'morj_qkv_post', q_lin.data_ptr(), qd, R, hq, 0, has_v, d, layer['q_norm'].data_ptr(),
-                 layer['k_norm'].data_ptr(), t.ptr('ro_positions'), self.inv_freq[kind].data_ptr(), None, eps,
-                 q.data_ptr(), None, None, s)
+        self._qkv(hr, layer, 0, R, hq, 0, has_v, d, kind, t.ptr('ro_positions'), None, q, None, None)
         attn = torch.empty(R, qd, dtype=bf, device=dev)
         self._attention(q, k_pool, v_pool, attn, t, 'ro_qo', 'ro_kv_indptr', 'ro_kv_indices', R, 0, kind, 'ro_work',
                         n_work['ro'])

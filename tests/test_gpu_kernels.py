@@ -305,3 +305,39 @@ def test_row_gather_scatter_and_reference_geglu():
     nat.call('morj_geglu', gd.data_ptr(), 33, 200, out.data_ptr(), stream())
     torch.cuda.synchronize()
     close(out, geglu(gu))
+
+
+@pytest.mark.parametrize('M,H,d,hq,hk,has_v', [(77, 256, 64, 4, 2, 1), (300, 256, 64, 4, 2, 0),
+                                               (2040, 5376, 128, 32, 16, 1), (517, 5376, 128, 32, 16, 0),
+                                               (9, 5376, 128, 32, 0, 1), (130, 512, 128, 0, 16, 0)])
+def test_fused_qkv_gemm_matches_gemm_then_oracle_head_epilogue(M, H, d, hq, hk, has_v):
+    """morj_gemm_qkv_rope == BF16 projection followed by the reference head epilogue (`_qkv_post`)."""
+    from oracle.lean_oracle import qkv_post, rope_tables
+    g = torch.Generator(device=DEV).manual_seed(M + hq)
+    rows = (hq + (2 if has_v else 1) * hk) * d
+    a = torch.randn(M, H, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(rows, H, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(d, device=DEV, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(d, device=DEV, generator=g)).to(torch.bfloat16)
+    pos = np.random.default_rng(M).integers(0, 9000, M)
+    inv = (1.0 / (10000 ** (torch.arange(0, d, 2).float() / d))).to(DEV)
+    cap = M + 5
+    slots = np.random.default_rng(M + 1).permutation(cap)[:M]
+    q_out = torch.zeros(M, max(hq, 1), d, device=DEV, dtype=torch.bfloat16)
+    kp = torch.zeros(cap, max(hk, 1), d, device=DEV, dtype=torch.bfloat16)
+    vp = torch.zeros(cap, max(hk, 1), d, device=DEV, dtype=torch.bfloat16)
+    pos_d, sl_d = i32(pos), i32(slots)
+    nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, has_v, d, qn.data_ptr(),
+             kn.data_ptr(), pos_d.data_ptr(), inv.data_ptr(), sl_d.data_ptr() if hk else None, 1e-6,
+             q_out.data_ptr() if hq else None, kp.data_ptr() if hk else None, vp.data_ptr() if hk else None, stream())
+    torch.cuda.synchronize()
+    proj = (a.float() @ w.float().T).bfloat16().cpu()
+    if hq == 0:  # the oracle's column layout always starts with q heads
+        proj = torch.cat([torch.zeros(M, 0, dtype=torch.bfloat16), proj], 1)
+    cos, sin = rope_tables(pos, inv.cpu())
+    q, k, v = qkv_post(proj, hq, hk, has_v, d, qn.cpu(), kn.cpu(), cos, sin, 1e-6, True)
+    if hq:
+        close(q_out, q)
+    if hk:
+        close(kp[torch.as_tensor(slots)], k)
+        close(vp[torch.as_tensor(slots)], v)

@@ -249,7 +249,8 @@ def kernel_arm(args):
         flops = 4 * case['hq'] * case['d'] * unmasked_pairs(qo, kv_len, window)
 
         def launch():
-            nat.call('morj_tree_attention', q.data_ptr(), kp.data_ptr(), vp.data_ptr(), out.data_ptr(), t[0].data_ptr(),
+            nat.call('morj_tree_attention', q.data_ptr(), q.shape[0], kp.data_ptr(), vp.data_ptr(), kp.shape[0],
+                     out.data_ptr(), t[0].data_ptr(),
                      t[1].data_ptr(), t[2].data_ptr(), t[3].data_ptr(), len(qo) - 1, 0, case['hq'], case['hk'],
                      case['d'], case['page_size'], window, float(case['sm_scale']), t[4].data_ptr(), nw, s)
         shape = dict(tokens=int(qo[-1]), window=window, pages=len(case['kv_indices']))

@@ -97,12 +97,12 @@ int morj_tree_attention_work(const int* qo_indptr_host, int n_segments, int hq, 
  * kv_len keys sees key t iff t <= kv_len - q_len + j (bottom-right causal) and, when window > 0,
  * t >= kv_len - q_len + j - (window - 1). The first n_bidir segments (image blocks) drop the causal bound and see
  * t >= kv_len - q_len + min(0, j - (window - 1)) (all keys when window <= 0).
- * q: [n, hq, d]; k_pool / v_pool: [slots, hk, d]; out: [n, hq, d]; scores are scaled by sm_scale.
+ * q: [n_q, hq, d]; k_pool / v_pool: [pool_slots, hk, d]; out: [n_q, hq, d]; scores are scaled by sm_scale.
  * GQA: query head h reads kv head h / (hq / hk). d in {64, 128}. work: pairs from morj_tree_attention_work. */
-int morj_tree_attention(const void* q, const void* k_pool, const void* v_pool, void* out, const int* qo_indptr,
-                        const int* kv_indptr, const int* kv_indices, const int* kv_last_page_len, int n_segments,
-                        int n_bidir, int hq, int hk, int d, int page_size, int window, float sm_scale,
-                        const int* work, int n_work, void* stream);
+int morj_tree_attention(const void* q, int n_q, const void* k_pool, const void* v_pool, int pool_slots, void* out,
+                        const int* qo_indptr, const int* kv_indptr, const int* kv_indices,
+                        const int* kv_last_page_len, int n_segments, int n_bidir, int hq, int hk, int d,
+                        int page_size, int window, float sm_scale, const int* work, int n_work, void* stream);
 
 /* Per row: o' = bf16(rmsnorm(o) * w_post); x = bf16(x + o'); h = bf16(rmsnorm(x) * w_pre). */
 int morj_attn_epilogue(const void* o, void* x, void* h_out, const void* w_post, const void* w_pre, int n, int H,

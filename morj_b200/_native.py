@@ -32,7 +32,7 @@ SIGNATURES = {
     'morj_embed_rmsnorm': [P, P, P, P, I, I, F, P, F, P, P, P],
     'morj_qkv_post': [P, LL, I, I, I, I, I, P, P, P, P, P, F, P, P, P, P],
     'morj_tree_attention_work': [IP, I, I, I, IP, I],
-    'morj_tree_attention': [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, F, P, I, P],
+    'morj_tree_attention': [P, I, P, P, I, P, P, P, P, P, I, I, I, I, I, I, I, F, P, I, P],
     'morj_attn_epilogue': [P, P, P, P, P, I, I, F, P],
     'morj_mlp_epilogue': [P, P, P, P, P, P, I, I, F, I, P],
     'morj_gather_rows': [P, LL, P, I, I, P, LL, P],

@@ -2,11 +2,13 @@
 //
 // One CTA handles one work tile: a segment's block of 128/G consecutive queries for one KV head, the G = hq/hk query
 // heads that share that KV head packed into the 128 MMA rows (row = query * G + head). The CTA is warp-specialised:
-//   warp 0      loader: gathers the K and V rows of each 64-key chunk from the paged pool (slot = page * page_size +
-//               offset) into 128-byte-swizzled shared memory with cp.async, two chunks in flight
+//   warp 0      K loader: the Q tile (TMA), then each 64-key chunk's K rows into a two-deep ring: one TMA tile load
+//               per head-dim half when the chunk's pool slots are contiguous (tree nodes own contiguous slot runs;
+//               pages hold 64 slots), a cp.async row gather otherwise
 //   warp 1      MMA issuer (one thread): S_c = Q K_c^T into one of two TMEM score buffers, then O += P_{c-1} V_{c-1}
 //               into the TMEM output, so the tensor cores compute chunk c+1's scores while the softmax works on c
-//   warps 2-5   softmax (thread = row): tree mask (bottom-right causal bound, sliding window, image-block rule), online
+//   warp 2      V loader: the same for V, on its own ring (K of chunk c+2 is fetched as soon as S_c is done)
+//   warps 4-7   softmax (thread = row): tree mask (bottom-right causal bound, sliding window, image-block rule), online
 //               softmax in FP32 with a lazily rescaled running maximum (O in TMEM is rescaled only when a row's
 //               maximum grows by more than 2^8), P as BF16 to shared memory, and the final O / l store
 // V is read as an N-major operand, so one shared-memory layout serves K (for QK^T) and V (for PV). The key range of a
@@ -18,7 +20,7 @@ namespace attn {
 
 constexpr int ROWS = 128;
 constexpr int BN = 64;
-constexpr int THREADS = 192;
+constexpr int THREADS = 256;
 constexpr int TMEM_COLS = 256;  // S buffers at columns [0, 64) and [64, 128), O at [128, 128 + D)
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_LOG2 = 8.0f;  // rescale O only when a row maximum grows by more than 2^8
@@ -33,9 +35,10 @@ struct Smem {
   static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;  // 2 buffers
   static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
   static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  // barriers: kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full, o_done, done; then the TMEM slot and abort flag.
-  // The dynamic shared window starts 1024-byte aligned (checked in the kernel), so two CTAs fit an SM.
-  static constexpr int TOTAL = BAR_OFF + 128;
+  // barriers (8 B each): q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full, o_done,
+  // done; then the TMEM slot and the abort flag. The dynamic shared window starts 1024-byte aligned (checked in the
+  // kernel), so two CTAs fit an SM.
+  static constexpr int TOTAL = BAR_OFF + 160;
 };
 
 MORJ_DEV void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
@@ -64,30 +67,50 @@ MORJ_DEV bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// one warp gathers the K and V rows of keys [t0, t0 + BN) (zeros past t_end) into one buffer pair
+// One loader warp fills buffer `dst` with the rows of keys [t0, t0 + BN) of one pool (K or V) for KV head h and
+// completes `full`: one TMA tile load per 64-column half when the 64 slots are consecutive and all keys are inside
+// the list, otherwise a cp.async row gather with zeros past t_end (so a masked key never brings a NaN into P V).
 template <int D>
-MORJ_DEV void load_kv_chunk(uint32_t k_dst, uint32_t v_dst, const __nv_bfloat16* __restrict__ k_pool,
-                            const __nv_bfloat16* __restrict__ v_pool, const int* __restrict__ kv_indices,
-                            const Segment& sg, int t0, int t_end, int hk, int h, int page_size, int lane) {
+MORJ_DEV void load_chunk(uint32_t dst, uint32_t full, const CUtensorMap* map, const __nv_bfloat16* __restrict__ pool,
+                         const int* __restrict__ kv_indices, const Segment& sg, int t0, int t_end, int hk, int h,
+                         int page_size, int lane) {
+  const int ta = t0 + 2 * lane, tb = ta + 1;
+  const int sa = ta < t_end ? key_slot(kv_indices, sg.kv_base, ta, page_size) : -1;
+  const int sb = tb < t_end ? key_slot(kv_indices, sg.kv_base, tb, page_size) : -1;
+  const int s0 = __shfl_sync(0xffffffffu, sa, 0);
+  const bool contiguous = __all_sync(0xffffffffu, sa == s0 + 2 * lane && sb == s0 + 2 * lane + 1);
+  if (contiguous) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(full, BN * D * 2);
+#pragma unroll
+      for (int half = 0; half < D / 64; ++half) tma_load_3d(dst + half * (BN * 128), map, full, half * 64, h, s0);
+    }
+    return;
+  }
   constexpr int CH = D / 8;  // 16-byte chunks per row
-  for (int k = lane; k < BN; k += 32) {
-    const int t = t0 + k;
-    const bool ok = t < t_end;
-    const size_t row = ok ? ((size_t)key_slot(kv_indices, sg.kv_base, t, page_size) * hk + h) * D : 0;
-    const __nv_bfloat16* ks = k_pool + row;
-    const __nv_bfloat16* vs = v_pool + row;
+#pragma unroll
+  for (int k2 = 0; k2 < 2; ++k2) {
+    const int k = 2 * lane + k2;
+    const int slot = k2 ? sb : sa;
+    const bool ok = slot >= 0;
+    const __nv_bfloat16* src = pool + (ok ? ((size_t)slot * hk + h) * D : 0);
 #pragma unroll
     for (int c16 = 0; c16 < CH; ++c16) {
       const uint32_t off = (uint32_t)((c16 >> 3) * (BN * 128)) + sw128_offset(k, c16 & 7);
-      cp_async16(k_dst + off, ks + c16 * 8, ok ? 16u : 0u);
-      cp_async16(v_dst + off, vs + c16 * 8, ok ? 16u : 0u);
+      cp_async16(dst + off, src + c16 * 8, ok ? 16u : 0u);
     }
   }
+  cp_async_commit();
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(full);
 }
 
 template <int D>
 __global__ void __launch_bounds__(THREADS, 2)
-    tree_attention_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_pool,
+    tree_attention_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                          const __grid_constant__ CUtensorMap v_map, const __nv_bfloat16* __restrict__ k_pool,
                           const __nv_bfloat16* __restrict__ v_pool, __nv_bfloat16* __restrict__ out,
                           const int* __restrict__ qo_indptr, const int* __restrict__ kv_indptr,
                           const int* __restrict__ kv_indices, const int* __restrict__ kv_last_page_len, int n_bidir,
@@ -100,10 +123,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     return;
   }
   const uint32_t bar0 = sbase + L::BAR_OFF;
-  const uint32_t kv_full = bar0, kv_empty = bar0 + 16, s_full = bar0 + 32, s_free = bar0 + 48;
-  const uint32_t p_full = bar0 + 64, o_done = bar0 + 72, done = bar0 + 80;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 96);
-  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 100);
+  const uint32_t q_full = bar0, k_full = bar0 + 8, v_full = bar0 + 24, k_empty = bar0 + 40, v_empty = bar0 + 56;
+  const uint32_t s_full = bar0 + 72, s_free = bar0 + 88, p_full = bar0 + 104, o_done = bar0 + 112, done = bar0 + 120;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 128);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 132);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int seg = work[2 * blockIdx.x], q0 = work[2 * blockIdx.x + 1];
@@ -122,7 +145,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int q_last = min(q0 + QT, sg.q_len) - 1;  // last valid query of the tile
   const int diag = sg.kv_len - sg.q_len;          // key aligned with query 0
 
-  // key range the tile can see
+  // key range the tile can see; the start is rounded down to a chunk boundary so chunks line up with 64-slot pages
   int t_begin, t_end;
   if (bidir) {
     t_end = sg.kv_len;
@@ -131,12 +154,16 @@ __global__ void __launch_bounds__(THREADS, 2)
     t_end = diag + q_last + 1;
     t_begin = window > 0 ? max(0, diag + q0 - (window - 1)) : 0;
   }
+  t_begin -= t_begin % BN;
   const int n_chunks = (t_end - t_begin + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(kv_full + 8 * b, 1);
-      mbar_init(kv_empty + 8 * b, 1);
+      mbar_init(k_full + 8 * b, 1);
+      mbar_init(v_full + 8 * b, 1);
+      mbar_init(k_empty + 8 * b, 1);
+      mbar_init(v_empty + 8 * b, 1);
       mbar_init(s_full + 8 * b, 1);
       mbar_init(s_free + 8 * b, 4);
     }
@@ -155,52 +182,36 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------- loader ----------------
-    // chunk c goes to buffer c & 1; chunk 0's copy group also carries the Q tile
-    constexpr int CH = D / 8;
-    for (int id = lane; id < ROWS * CH; id += 32) {
-      const int r = id / CH, c16 = id % CH;
-      const int qi = q0 + r / G;
-      const bool ok = qi < sg.q_len;
-      const size_t src = ok ? ((size_t)(sg.q_start + qi) * hq + h * G + r % G) * D : 0;
-      const uint32_t off = (uint32_t)((c16 >> 3) * (ROWS * 128)) + sw128_offset(r, c16 & 7);
-      cp_async16(sbase + L::Q_OFF + off, q + src + c16 * 8, ok ? 16u : 0u);
+  if (warp == 0 || warp == 2) {
+    // ---------------- K loader (warp 0) / V loader (warp 2) ----------------
+    const bool is_k = warp == 0;
+    if (is_k && lane == 0) {
+      tma_prefetch(&q_map);
+      tma_prefetch(&k_map);
+      // Q tile: rows (query, head) of queries [q0, q0 + QT) and heads [h * G, h * G + G); rows past the tensor read 0
+      mbar_arrive_expect_tx(q_full, ROWS * D * 2);
+#pragma unroll
+      for (int half = 0; half < D / 64; ++half)
+        tma_load_3d(sbase + L::Q_OFF + half * (ROWS * 128), &q_map, q_full, half * 64, h * G, sg.q_start + q0);
     }
-    // Chunk c is published (kv_full) as soon as it has landed, before the loader waits for a buffer to reuse: the
-    // issuer needs chunk c's keys to run S_c and then PV_{c-1}, and that PV is what frees the buffer of chunk c + 1.
-    load_kv_chunk<D>(sbase + L::K_OFF, sbase + L::V_OFF, k_pool, v_pool, kv_indices, sg, t_begin, t_end, hk, h,
-                     page_size, lane);
-    cp_async_commit();
-    bool ok = true;
-    for (int c = 1; c < n_chunks; ++c) {
-      cp_async_wait<0>();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(kv_full + 8 * ((c - 1) & 1));
+    if (!is_k && lane == 0) tma_prefetch(&v_map);
+    const uint32_t base = sbase + (is_k ? L::K_OFF : L::V_OFF);
+    const uint32_t full = is_k ? k_full : v_full, empty = is_k ? k_empty : v_empty;
+    for (int c = 0; c < n_chunks; ++c) {
       const int b = c & 1;
-      if (c >= 2 && !warp_wait(kv_empty + 8 * b, ((c >> 1) - 1) & 1, abort)) {
-        ok = false;
-        break;
-      }
-      load_kv_chunk<D>(sbase + L::K_OFF + b * L::KV_BYTES, sbase + L::V_OFF + b * L::KV_BYTES, k_pool, v_pool,
-                       kv_indices, sg, t_begin + c * BN, t_end, hk, h, page_size, lane);
-      cp_async_commit();
-    }
-    cp_async_wait<0>();
-    if (ok) {
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(kv_full + 8 * ((n_chunks - 1) & 1));
+      if (c >= 2 && !warp_wait(empty + 8 * b, ((c >> 1) - 1) & 1, abort)) break;
+      load_chunk<D>(base + b * L::KV_BYTES, full + 8 * b, is_k ? &k_map : &v_map, is_k ? k_pool : v_pool,
+                    kv_indices, sg, t_begin + c * BN, t_end, hk, h, page_size, lane);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16(ROWS, BN);
       constexpr uint32_t IDESC_O = idesc_bf16(ROWS, D, /*b_mn_major=*/true);
-      bool ok = true;
+      bool ok = mbar_wait(q_full, 0, abort, kErrTimeoutAttention);
       auto issue_pv = [&](int j) -> bool {
         if (!mbar_wait(p_full, j & 1, abort, kErrTimeoutAttention)) return false;
+        if (!mbar_wait(v_full + 8 * (j & 1), (j >> 1) & 1, abort, kErrTimeoutAttention)) return false;
         tc_fence_after();
         const uint32_t v_s = sbase + L::V_OFF + (j & 1) * L::KV_BYTES;
 #pragma unroll
@@ -210,12 +221,12 @@ __global__ void __launch_bounds__(THREADS, 2)
           umma_bf16(tmem + 128, sw128_desc(pa), sw128_desc(vb, BN * 128), IDESC_O, (j | kk) != 0);
         }
         umma_commit(o_done);
-        umma_commit(kv_empty + 8 * (j & 1));
+        umma_commit(v_empty + 8 * (j & 1));
         return true;
       };
       for (int c = 0; c < n_chunks && ok; ++c) {
         const int b = c & 1;
-        if (!mbar_wait(kv_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention)) {
+        if (!mbar_wait(k_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention)) {
           ok = false;
           break;
         }
@@ -232,6 +243,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           umma_bf16(tmem + b * BN, sw128_desc(qa), sw128_desc(kb), IDESC_S, kk > 0);
         }
         umma_commit(s_full + 8 * b);
+        umma_commit(k_empty + 8 * b);
         if (c >= 1) ok = issue_pv(c - 1);
       }
       if (ok) issue_pv(n_chunks - 1);
@@ -239,7 +251,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       umma_commit(done);
       mbar_wait_landed(done, 0);
     }
-  } else {
+  } else if (warp >= 4) {
     // ---------------- softmax warpgroup ----------------
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. + 31
     const int r = quarter * 32 + lane;
@@ -355,6 +367,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
     }
   }
+  // (warp 3 has no role)
 
   tc_fence_before();
   __syncthreads();
@@ -365,9 +378,9 @@ __global__ void __launch_bounds__(THREADS, 2)
 }
 
 template <int D>
-static int launch(const void* q, const void* k_pool, const void* v_pool, void* out, const int* qo_indptr,
-                  const int* kv_indptr, const int* kv_indices, const int* kv_last_page_len, int n_bidir, int hq,
-                  int hk, int page_size, int window, float sm_scale, const int* work, int n_work,
+static int launch(const void* q, int n_q, const void* k_pool, const void* v_pool, int pool_slots, void* out,
+                  const int* qo_indptr, const int* kv_indptr, const int* kv_indices, const int* kv_last_page_len,
+                  int n_bidir, int hq, int hk, int page_size, int window, float sm_scale, const int* work, int n_work,
                   cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
@@ -376,11 +389,30 @@ static int launch(const void* q, const void* k_pool, const void* v_pool, void* o
     if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = true;
   }
+  const int G = hq / hk;
+  CUtensorMap qm, km, vm;
+  {  // q [n_q, hq, D]: box = 64 columns x G heads x 128/G queries
+    const unsigned long long dims[3] = {(unsigned long long)D, (unsigned long long)hq, (unsigned long long)n_q};
+    const unsigned long long strides[2] = {(unsigned long long)D * 2, (unsigned long long)hq * D * 2};
+    const unsigned box[3] = {64u, (unsigned)G, (unsigned)(ROWS / G)};
+    int st = encode_tiled(&qm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
+  {  // pools [slots, hk, D]: box = 64 columns x 1 head x 64 slots
+    const unsigned long long dims[3] = {(unsigned long long)D, (unsigned long long)hk, (unsigned long long)pool_slots};
+    const unsigned long long strides[2] = {(unsigned long long)D * 2, (unsigned long long)hk * D * 2};
+    const unsigned box[3] = {64u, 1u, (unsigned)BN};
+    int st = encode_tiled(&km, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k_pool, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_tiled(&vm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v_pool, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
   dim3 grid(n_work, hk);
   tree_attention_kernel<D><<<grid, THREADS, Smem<D>::TOTAL, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k_pool),
-      reinterpret_cast<const __nv_bfloat16*>(v_pool), reinterpret_cast<__nv_bfloat16*>(out), qo_indptr, kv_indptr,
-      kv_indices, kv_last_page_len, n_bidir, hq, hk, page_size, window, sm_scale * LOG2E, work);
+      qm, km, vm, reinterpret_cast<const __nv_bfloat16*>(k_pool), reinterpret_cast<const __nv_bfloat16*>(v_pool),
+      reinterpret_cast<__nv_bfloat16*>(out), qo_indptr, kv_indptr, kv_indices, kv_last_page_len, n_bidir, hq, hk,
+      page_size, window, sm_scale * LOG2E, work);
   return check_launch("tree_attention_kernel");
 }
 
@@ -419,25 +451,29 @@ extern "C" int morj_tree_attention_work(const int* qo_indptr_host, int n_segment
   return n;
 }
 
-extern "C" int morj_tree_attention(const void* q, const void* k_pool, const void* v_pool, void* out,
-                                   const int* qo_indptr, const int* kv_indptr, const int* kv_indices,
+extern "C" int morj_tree_attention(const void* q, int n_q, const void* k_pool, const void* v_pool, int pool_slots,
+                                   void* out, const int* qo_indptr, const int* kv_indptr, const int* kv_indices,
                                    const int* kv_last_page_len, int n_segments, int n_bidir, int hq, int hk, int d,
                                    int page_size, int window, float sm_scale, const int* work, int n_work,
                                    void* stream) {
   using namespace morj;
   if (n_work == 0 || n_segments == 0) return MORJ_OK;
-  if (!q || !k_pool || !v_pool || !out || !qo_indptr || !kv_indptr || !kv_indices || !work || n_work < 0)
-    return set_error(MORJ_ERR_ARG, "morj_tree_attention: null pointer or negative size");
+  if (!q || !k_pool || !v_pool || !out || !qo_indptr || !kv_indptr || !kv_indices || !work || n_work < 0 ||
+      n_q <= 0 || pool_slots <= 0)
+    return set_error(MORJ_ERR_ARG, "morj_tree_attention: null pointer or bad size");
   if (hq <= 0 || hk <= 0 || hq % hk || attn::ROWS % (hq / hk))
     return set_error(MORJ_ERR_ARG, "morj_tree_attention: hq=%d hk=%d unsupported", hq, hk);
   if (page_size <= 0 || n_bidir < 0 || n_bidir > n_segments)
     return set_error(MORJ_ERR_ARG, "morj_tree_attention: bad page_size %d or n_bidir %d", page_size, n_bidir);
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool)) &
+      15)
+    return set_error(MORJ_ERR_ARG, "morj_tree_attention: q and pools must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (d == 128)
-    return attn::launch<128>(q, k_pool, v_pool, out, qo_indptr, kv_indptr, kv_indices, kv_last_page_len, n_bidir, hq,
-                             hk, page_size, window, sm_scale, work, n_work, s);
+    return attn::launch<128>(q, n_q, k_pool, v_pool, pool_slots, out, qo_indptr, kv_indptr, kv_indices,
+                             kv_last_page_len, n_bidir, hq, hk, page_size, window, sm_scale, work, n_work, s);
   if (d == 64)
-    return attn::launch<64>(q, k_pool, v_pool, out, qo_indptr, kv_indptr, kv_indices, kv_last_page_len, n_bidir, hq,
-                            hk, page_size, window, sm_scale, work, n_work, s);
+    return attn::launch<64>(q, n_q, k_pool, v_pool, pool_slots, out, qo_indptr, kv_indptr, kv_indices,
+                            kv_last_page_len, n_bidir, hq, hk, page_size, window, sm_scale, work, n_work, s);
   return set_error(MORJ_ERR_UNSUPPORTED, "morj_tree_attention: head_dim %d unsupported (64, 128)", d);
 }

@@ -110,6 +110,13 @@ MORJ_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, in
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+MORJ_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 MORJ_DEV uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -240,5 +247,10 @@ MORJ_DEV float gelu_tanh(float x) {
 // host side: status and the calling thread's last error message (rowops.cu)
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
+
+// host side: tiled tensor maps (driver entry point resolved at run time; gemm_sm100.cu)
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* ptr, const unsigned long long* dims,
+                 const unsigned long long* strides_bytes, const unsigned* box, CUtensorMapSwizzle swizzle);
+int num_sms();
 
 }  // namespace morj

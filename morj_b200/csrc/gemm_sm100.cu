@@ -400,22 +400,27 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2D BF16 tensor map over a row-major [rows, cols] matrix with leading dimension ld, box [box_rows, 64 cols].
-static int make_map(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld, int box_rows) {
-  EncodeTiledFn fn = encode_fn();
+}  // namespace gemm
+
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* ptr, const unsigned long long* dims,
+                 const unsigned long long* strides_bytes, const unsigned* box, CUtensorMapSwizzle swizzle) {
+  gemm::EncodeTiledFn fn = gemm::encode_fn();
   if (!fn) return set_error(MORJ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, type, rank, const_cast<void*>(ptr), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(MORJ_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return MORJ_OK;
 }
 
-static int num_sms() {
+int num_sms() {
   static int n = 0;
   if (n == 0) {
     int dev = 0;
@@ -424,6 +429,16 @@ static int num_sms() {
     if (n <= 0) n = 148;
   }
   return n;
+}
+
+namespace gemm {
+
+// 2D BF16 tensor map over a row-major [rows, cols] matrix with leading dimension ld, box [box_rows, 64 cols].
+static int make_map(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld, int box_rows) {
+  const unsigned long long dims[2] = {(unsigned long long)cols, (unsigned long long)rows};
+  const unsigned long long strides[1] = {(unsigned long long)(ld * 2)};
+  const unsigned box[2] = {(unsigned)BK, (unsigned)box_rows};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <int EPI, int BN>

@@ -563,9 +563,9 @@ class LeanGemma4:
     def _attention(self, q, k_pool, v_pool, out, t, qo, kv_indptr, kv_indices, n_seg, n_bidir, kind, work, n_work):
         hk, d = self.geom[kind]
         window = self.window if kind == 'sliding_attention' else 0
-        self._k('attention', 'morj_tree_attention', q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), out.data_ptr(),
-                 t.ptr(qo), t.ptr(kv_indptr), t.ptr(kv_indices), None, n_seg, n_bidir, self.hq, hk, d, 1, window,
-                 1.0, t.ptr(work), n_work, self._stream())
+        self._k('attention', 'morj_tree_attention', q.data_ptr(), q.shape[0], k_pool.data_ptr(), v_pool.data_ptr(),
+                k_pool.shape[0], out.data_ptr(), t.ptr(qo), t.ptr(kv_indptr), t.ptr(kv_indices), None, n_seg, n_bidir,
+                self.hq, hk, d, 1, window, 1.0, t.ptr(work), n_work, self._stream())
 
     def _step(self, k, st, plan, pools, head, req, tables):
         """One forward over a planned step (reference `lean_core.py:599-694`); returns (the residual rows of the

@@ -134,7 +134,8 @@ def _run_attention(case, n_bidir=0, window=0, device_tables=True):
     last = case.get('last_page_len')
     last_d = i32(last) if last is not None else None
     t = [i32(qo), i32(case['kv_indptr']), i32(case['kv_indices']), i32(work[:2 * nw])]
-    nat.call('morj_tree_attention', q.data_ptr(), kp.data_ptr(), vp.data_ptr(), out.data_ptr(), t[0].data_ptr(),
+    nat.call('morj_tree_attention', q.data_ptr(), q.shape[0], kp.data_ptr(), vp.data_ptr(), kp.shape[0],
+             out.data_ptr(), t[0].data_ptr(),
              t[1].data_ptr(), t[2].data_ptr(), last_d.data_ptr() if last_d is not None else None, len(qo) - 1, n_bidir,
              hq, hk, d, case['page_size'], window, float(case['sm_scale']), t[3].data_ptr(), nw, stream())
     torch.cuda.synchronize()

@@ -288,28 +288,37 @@ __global__ void __launch_bounds__(THREADS, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free + 8 * b);
       const int t0 = t_begin + c * BN;
+      // Scores are kept raw; the softmax works in the log2 domain with the scale folded into one FMA per element.
+      // Chunks every key of which this row sees (the bulk of a long prefix) skip the per-key mask.
+      const bool full = t0 >= lo && t0 + BN - 1 <= hi;
       float mx = -INFINITY;
+      if (__all_sync(0xffffffffu, full)) {
 #pragma unroll
-      for (int j = 0; j < BN; ++j) {
-        const int t = t0 + j;
-        const float v = (t >= lo && t <= hi) ? __uint_as_float(sr[j >> 5][j & 31]) * scale_log2 : -INFINITY;
-        sr[j >> 5][j & 31] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int j = 0; j < BN; ++j) mx = fmaxf(mx, __uint_as_float(sr[j >> 5][j & 31]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int t = t0 + j;
+          const float v = (t >= lo && t <= hi) ? __uint_as_float(sr[j >> 5][j & 31]) : -INFINITY;
+          sr[j >> 5][j & 31] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
       }
+      mx *= scale_log2;  // scale > 0: the maximum of the scaled scores
       float alpha = 1.f;
       if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
         if (m_used != -INFINITY) alpha = fast_exp2(m_used - mx);
         if (mx != -INFINITY) m_used = mx;
       }
       l_run *= alpha;
+      // exp2(-inf) = 0 for masked keys; a row with no visible key yet keeps m_used = -inf and p = 0
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
       float psum = 0.f;
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int j = 0; j < BN; j += 2) {
-        const float s0 = __uint_as_float(sr[j >> 5][j & 31]);
-        const float s1 = __uint_as_float(sr[(j + 1) >> 5][(j + 1) & 31]);
-        const float p0 = s0 == -INFINITY ? 0.f : fast_exp2(s0 - m_used);
-        const float p1 = s1 == -INFINITY ? 0.f : fast_exp2(s1 - m_used);
+        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[j >> 5][j & 31]), scale_log2, neg_m));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[(j + 1) >> 5][(j + 1) & 31]), scale_log2, neg_m));
         psum += p0 + p1;
         pk[j / 2] = pack_bf16x2(p0, p1);
       }

@@ -239,11 +239,11 @@ def kernel_arm(args):
         q, kp, vp = case['q'].to(dev), case['k_pool'].to(dev), case['v_pool'].to(dev)
         out = torch.empty_like(q)
         qo = case['qo_indptr']
-        work = np.zeros(2 * 4096, np.int32)
-        nw = nat.lib().morj_tree_attention_work(np.ascontiguousarray(qo).ctypes.data_as(nat.IP), len(qo) - 1,
-                                                case['hq'], case['hk'], work.ctypes.data_as(nat.IP), 4096)
+        work = nat.attention_work(qo, case['kv_indptr'], 0, case['hq'], case['hk'], window, case['page_size'],
+                                  case['last_page_len'])
+        nw = len(work) // 2
         t = [torch.as_tensor(x, device=dev) for x in (qo, case['kv_indptr'], case['kv_indices'],
-                                                       case['last_page_len'], work[:2 * nw])]
+                                                       case['last_page_len'], work)]
         kv_len = [(case['kv_indptr'][i + 1] - case['kv_indptr'][i] - 1) * case['page_size'] + case['last_page_len'][i]
                   for i in range(len(qo) - 1)]
         flops = 4 * case['hq'] * case['d'] * unmasked_pairs(qo, kv_len, window)

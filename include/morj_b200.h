@@ -86,10 +86,13 @@ int morj_qkv_post(const void* qkv, long long ld, int n, int hq, int hk, int has_
                   const void* k_norm, const int* positions, const float* inv_freq, const int* slots, float eps,
                   void* q_out, void* k_pool, void* v_pool, void* stream);
 
-/* Work list for morj_tree_attention (host function, no device access): splits each segment's queries
- * (qo_indptr_host, n_segments + 1 entries) into tiles of 128 / (hq / hk) queries; writes up to `cap`
- * (segment, first query) int pairs to work_host and returns the number of tiles (-1 if cap is too small). */
-int morj_tree_attention_work(const int* qo_indptr_host, int n_segments, int hq, int hk, int* work_host, int cap);
+/* Work list for morj_tree_attention (host function, no device access): splits each segment's queries into tiles of
+ * 128 / (hq / hk) queries and orders the tiles by the number of 64-key chunks they walk, longest first, from the host
+ * copies of the attention call's segment tables (same meaning as there). Writes up to `cap` (segment, first query)
+ * int pairs to work_host and returns the number of tiles (-1 if cap is too small). */
+int morj_tree_attention_work(const int* qo_indptr_host, const int* kv_indptr_host, const int* kv_last_page_len_host,
+                             int n_segments, int n_bidir, int hq, int hk, int page_size, int window, int* work_host,
+                             int cap);
 
 /* Tree-masked paged prefill attention. Segment s owns queries [qo_indptr[s], qo_indptr[s+1]) and the key list
  * pages kv_indices[kv_indptr[s] .. kv_indptr[s+1]) of page_size slots each (the last page holds

@@ -31,7 +31,7 @@ SIGNATURES = {
     'morj_gemm_qkv_rope': [P, LL, P, LL, I, I, I, I, I, I, P, P, P, P, P, F, P, P, P, P],
     'morj_embed_rmsnorm': [P, P, P, P, I, I, F, P, F, P, P, P],
     'morj_qkv_post': [P, LL, I, I, I, I, I, P, P, P, P, P, F, P, P, P, P],
-    'morj_tree_attention_work': [IP, I, I, I, IP, I],
+    'morj_tree_attention_work': [IP, IP, IP, I, I, I, I, I, I, IP, I],
     'morj_tree_attention': [P, I, P, P, I, P, P, P, P, P, I, I, I, I, I, I, I, F, P, I, P],
     'morj_attn_epilogue': [P, P, P, P, P, I, I, F, P],
     'morj_mlp_epilogue': [P, P, P, P, P, P, I, I, F, I, P],
@@ -79,6 +79,24 @@ def check(status, what):
 def call(name, *args):
     """Call entry point `name` and raise on a non-zero status."""
     check(getattr(lib(), name)(*args), name)
+
+
+def attention_work(qo_indptr, kv_indptr, n_bidir, hq, hk, window, page_size=1, kv_last_page_len=None):
+    """The attention work list (int32 pairs, longest tiles first) for host copies of a call's segment tables."""
+    import numpy as np
+    qo = np.ascontiguousarray(qo_indptr, dtype=np.int32)
+    kv = np.ascontiguousarray(kv_indptr, dtype=np.int32)
+    last = None if kv_last_page_len is None else np.ascontiguousarray(kv_last_page_len, dtype=np.int32)
+    n_seg = len(qo) - 1
+    qt = 128 // (hq // hk)
+    cap = max(1, int(sum((int(qo[i + 1] - qo[i]) + qt - 1) // qt for i in range(n_seg))))
+    buf = np.zeros(2 * cap, dtype=np.int32)
+    got = lib().morj_tree_attention_work(qo.ctypes.data_as(IP), kv.ctypes.data_as(IP),
+                                         last.ctypes.data_as(IP) if last is not None else None, n_seg, n_bidir, hq, hk,
+                                         page_size, window, buf.ctypes.data_as(IP), cap)
+    if got < 0:
+        check(ERR_ARG, 'morj_tree_attention_work')
+    return buf[:2 * got]
 
 
 def device_error(stream, clear=True):

@@ -13,6 +13,10 @@
 //               maximum grows by more than 2^8), P as BF16 to shared memory, and the final O / l store
 // V is read as an N-major operand, so one shared-memory layout serves K (for QK^T) and V (for PV). The key range of a
 // tile is cut to what its queries can see, so a sliding layer's long prefix costs O(window) per tile.
+#include <algorithm>
+#include <array>
+#include <vector>
+
 #include "common.cuh"
 
 namespace morj {
@@ -428,10 +432,11 @@ static int launch(const void* q, int n_q, const void* k_pool, const void* v_pool
 }  // namespace attn
 }  // namespace morj
 
-extern "C" int morj_tree_attention_work(const int* qo_indptr_host, int n_segments, int hq, int hk, int* work_host,
-                                        int cap) {
+extern "C" int morj_tree_attention_work(const int* qo_indptr_host, const int* kv_indptr_host,
+                                        const int* kv_last_page_len_host, int n_segments, int n_bidir, int hq, int hk,
+                                        int page_size, int window, int* work_host, int cap) {
   using namespace morj;
-  if (!qo_indptr_host || n_segments < 0 || hk <= 0 || hq <= 0 || hq % hk) {
+  if (!qo_indptr_host || !kv_indptr_host || n_segments < 0 || hk <= 0 || hq <= 0 || hq % hk || page_size <= 0) {
     set_error(MORJ_ERR_ARG, "morj_tree_attention_work: bad arguments");
     return -1;
   }
@@ -441,21 +446,43 @@ extern "C" int morj_tree_attention_work(const int* qo_indptr_host, int n_segment
     return -1;
   }
   const int QT = attn::ROWS / G;
-  int n = 0;
-  // within a segment, later tiles first: they see the most keys under the causal mask
+  // every tile with the number of key chunks it will walk (the same range the kernel computes)
+  std::vector<std::array<int, 3>> tiles;  // (chunks, segment, first query)
   for (int s = 0; s < n_segments; ++s) {
-    const int len = qo_indptr_host[s + 1] - qo_indptr_host[s];
-    for (int q0 = ((len - 1) / QT) * QT; q0 >= 0 && len > 0; q0 -= QT) {
-      if (n < cap && work_host) {
-        work_host[2 * n] = s;
-        work_host[2 * n + 1] = q0;
+    const int q_len = qo_indptr_host[s + 1] - qo_indptr_host[s];
+    const int pages = kv_indptr_host[s + 1] - kv_indptr_host[s];
+    const int kv_len = page_size == 1 ? pages
+                                      : (pages - 1) * page_size +
+                                            (kv_last_page_len_host ? kv_last_page_len_host[s] : page_size);
+    const int diag = kv_len - q_len;
+    for (int q0 = 0; q0 < q_len; q0 += QT) {
+      const int q_last = std::min(q0 + QT, q_len) - 1;
+      int t_begin, t_end;
+      if (s < n_bidir) {
+        t_end = kv_len;
+        t_begin = window > 0 ? std::max(0, diag + std::min(0, q0 - (window - 1))) : 0;
+      } else {
+        t_end = diag + q_last + 1;
+        t_begin = window > 0 ? std::max(0, diag + q0 - (window - 1)) : 0;
       }
-      ++n;
+      t_begin -= t_begin % attn::BN;
+      tiles.push_back({(t_end - t_begin + attn::BN - 1) / attn::BN, s, q0});
     }
   }
+  const int n = (int)tiles.size();
   if (n > cap) {
     set_error(MORJ_ERR_ARG, "morj_tree_attention_work: %d tiles exceed capacity %d", n, cap);
     return -1;
+  }
+  // longest first: the grid's last wave then holds the short tiles
+  std::stable_sort(tiles.begin(), tiles.end(), [](const std::array<int, 3>& a, const std::array<int, 3>& b) {
+    return a[0] > b[0];
+  });
+  if (work_host) {
+    for (int i = 0; i < n; ++i) {
+      work_host[2 * i] = tiles[i][1];
+      work_host[2 * i + 1] = tiles[i][2];
+    }
   }
   return n;
 }

@@ -479,18 +479,6 @@ class LeanGemma4:
         self.trace.append((kind, flops, e0, e1))
 
     # ---- forward over one step ------------------------------------------------------------------------------------
-    def _work(self, qo, G):
-        n_seg = len(qo) - 1
-        qt = 128 // G
-        cap = int(sum((int(qo[i + 1] - qo[i]) + qt - 1) // qt for i in range(n_seg)))
-        buf = np.zeros(2 * max(cap, 1), dtype=np.int32)
-        qo_c = np.ascontiguousarray(qo, dtype=np.int32)
-        got = nat.lib().morj_tree_attention_work(qo_c.ctypes.data_as(nat.IP), n_seg, self.hq, self.hq // G,
-                                                 buf.ctypes.data_as(nat.IP), max(cap, 1))
-        if got < 0:
-            nat.check(nat.ERR_ARG, 'morj_tree_attention_work')
-        return buf[:2 * got]
-
     def _step_tables(self, k, st, plan, req):
         t = _Tables(self.device)
         n = len(st['tokens'])
@@ -504,7 +492,9 @@ class LeanGemma4:
         t.add('qo', qo)
         n_work = {}
         for kk, kind in (('s', 'sliding_attention'), ('g', 'full_attention')):
-            w = self._work(qo, self.hq // self.geom[kind][0])
+            sliding = kind == 'sliding_attention'
+            w = nat.attention_work(qo, st['kv_indptr_' + kk], int(st['n_bidir']) if sliding else 0, self.hq,
+                                   self.geom[kind][0], self.window if sliding else 0)
             t.add('work_' + kk, w)
             n_work[kk] = len(w) // 2
         if req.features is not None:
@@ -534,7 +524,9 @@ class LeanGemma4:
             t.add('ro_qo', np.arange(len(rows) + 1))
             t.add('ro_kv_indptr', ptr)
             t.add('ro_kv_indices', np.concatenate(ind))
-            ro_work = self._work(np.arange(len(rows) + 1, dtype=np.int32), self.hq // self.geom[self.types[-1]][0])
+            last_sliding = self.types[-1] == 'sliding_attention'
+            ro_work = nat.attention_work(np.arange(len(rows) + 1), ptr, 0, self.hq, self.geom[self.types[-1]][0],
+                                         self.window if last_sliding else 0)
             t.add('ro_work', ro_work)
             n_work['ro'] = len(ro_work) // 2
         t.upload()

@@ -126,14 +126,13 @@ def _run_attention(case, n_bidir=0, window=0, device_tables=True):
     kp, vp = case['k_pool'].to(DEV), case['v_pool'].to(DEV)
     out = torch.full(q.shape, float('nan'), device=DEV, dtype=torch.bfloat16)
     qo = case['qo_indptr']
-    cap = 4096
-    work = np.zeros(2 * cap, np.int32)
-    nw = nat.lib().morj_tree_attention_work(np.ascontiguousarray(qo, np.int32).ctypes.data_as(nat.IP), len(qo) - 1,
-                                            hq, hk, work.ctypes.data_as(nat.IP), cap)
+    work = nat.attention_work(qo, case['kv_indptr'], n_bidir, hq, hk, window, case['page_size'],
+                              case.get('last_page_len'))
+    nw = len(work) // 2
     assert nw > 0
     last = case.get('last_page_len')
     last_d = i32(last) if last is not None else None
-    t = [i32(qo), i32(case['kv_indptr']), i32(case['kv_indices']), i32(work[:2 * nw])]
+    t = [i32(qo), i32(case['kv_indptr']), i32(case['kv_indices']), i32(work)]
     nat.call('morj_tree_attention', q.data_ptr(), q.shape[0], kp.data_ptr(), vp.data_ptr(), kp.shape[0],
              out.data_ptr(), t[0].data_ptr(),
              t[1].data_ptr(), t[2].data_ptr(), last_d.data_ptr() if last_d is not None else None, len(qo) - 1, n_bidir,

@@ -41,15 +41,17 @@ def test_host_side_work_list_and_error_reporting():
     import ctypes
     import numpy as np
     lib = _native.lib()
+    # segments of 130, 1, 0 and 69 queries over 130, 200, 5 and 69 keys; 64 queries per tile (2 heads per KV head)
     qo = np.array([0, 130, 131, 131, 200], dtype=np.int32)
-    work = np.zeros(64, dtype=np.int32)
-    n = lib.morj_tree_attention_work(qo.ctypes.data_as(_native.IP), 4, 32, 16, work.ctypes.data_as(_native.IP), 32)
-    # 64 queries per tile for 2 query heads per KV head; within a segment the later tiles come first
-    assert n == 6
-    pairs = work[:2 * n].reshape(-1, 2).tolist()
-    assert pairs == [[0, 128], [0, 64], [0, 0], [1, 0], [3, 64], [3, 0]]
-    assert lib.morj_tree_attention_work(qo.ctypes.data_as(_native.IP), 4, 32, 16, work.ctypes.data_as(_native.IP), 2) == -1
-    assert b'exceed capacity' in lib.morj_last_error()
+    kv = np.array([0, 130, 330, 335, 404], dtype=np.int32)
+    work = _native.attention_work(qo, kv, 0, 32, 16, 0)
+    pairs = work.reshape(-1, 2).tolist()
+    assert sorted(pairs) == [[0, 0], [0, 64], [0, 128], [1, 0], [3, 0], [3, 64]]
+    # longest first: the segment-1 row sees 200 keys (4 chunks), segment 0's last tile 130 keys (3 chunks)
+    assert pairs[0] == [1, 0] and pairs[1] == [0, 128]
+    cap_fail = lib.morj_tree_attention_work(qo.ctypes.data_as(_native.IP), kv.ctypes.data_as(_native.IP), None, 4, 0,
+                                            32, 16, 1, 0, work.ctypes.data_as(_native.IP), 2)
+    assert cap_fail == -1 and b'exceed capacity' in lib.morj_last_error()
     # argument checks fail before any device access
     with pytest.raises(ValueError, match='multiples of 8'):
         _native.call('morj_gemm_bf16', 16, 7, 16, 7, 16, 16, 4, 16, 7, 0, None)

@@ -367,11 +367,26 @@ def main():
         clocks.stop()
         e2e_ms = e2.elapsed_time(e3) / args.steps
         h2d, d2h = model.h2d_bytes, model.d2h_bytes
+        # ---- the same planned pass captured once in a CUDA graph and replayed (launch gaps between kernels gone) ----
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            model.execute_pass(prepared)
+        graph.replay()
+        barrier()
+        e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e4.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e5.record()
+        barrier()
+        graph_ms = e4.elapsed_time(e5) / args.steps
+        del graph
         # ---- one traced step (CUDA events around every kernel) for the per-kernel roofline -----------------------
         model.trace = []
         model.execute_pass(prepared)
         torch.cuda.synchronize()
         trace, model.trace = model.trace, None
+        trace_span = trace[0][2].elapsed_time(trace[-1][3])
     per_kind = {}
     for kind, fl, a, b in trace:
         d = per_kind.setdefault(kind, dict(ms=0.0, launches=0, flops=0))
@@ -426,6 +441,7 @@ def main():
                           launches=len(big), avg_launch_us=round(1000 * g_ms / max(len(big), 1), 2),
                           all_gemms_tflops=round(all_tf, 1)),
             breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
+            traced_span_ms=round(trace_span, 3), graph_replay_ms=round(graph_ms, 3),
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
                      ms_per_step=e2e_max),
             gpu_launches=int(launches * args.steps),

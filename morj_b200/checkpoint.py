@@ -3,7 +3,10 @@
 Keys and shapes follow the checkpoint the reference engine loads (`aleria_judge/lean_core.py:360-382`: prefix
 `model.language_model.`, fused at load into `qkv` and `gate/up`), so the same directory loads into either engine.
 Random init (no real weights exist offline): linear and embedding weights N(0, std); RMSNorm weights and the
-per-layer scalar 1 + N(0, norm_std) (non-trivial, so a kernel that ignored them would fail parity).
+per-layer scalar 1 + N(0, norm_std) (non-trivial, so a kernel that ignored them would fail parity). The q and k norm
+weights are further scaled by head_dim^-1/4: the model attends with scale 1.0 (its q/k norms carry the scale), so
+unit q/k norm weights would give logits of standard deviation sqrt(head_dim) and a near one-hot, chaotic attention
+that no trained checkpoint has; scaled, the logits have unit variance.
 """
 import json
 import os
@@ -40,9 +43,11 @@ def tensor_shapes(top):
     return out
 
 
-def random_tensor(shape, gen, device, std=0.02, norm_std=0.1):
+def random_tensor(shape, gen, device, std=0.02, norm_std=0.1, key=''):
     if len(shape) == 1:  # norm weights and layer scalars
         t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * norm_std + 1.0
+        if key.endswith(('q_norm.weight', 'k_norm.weight')):
+            t = t * shape[0] ** -0.25
     else:
         t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
     return t.to(torch.bfloat16)
@@ -51,7 +56,7 @@ def random_tensor(shape, gen, device, std=0.02, norm_std=0.1):
 def random_state(top, seed=0, std=0.02, norm_std=0.1, device='cpu'):
     """Every tensor of `tensor_shapes(top)`, drawn in order from one seeded generator on `device`."""
     gen = torch.Generator(device=device).manual_seed(seed)
-    return {k: random_tensor(s, gen, device, std, norm_std) for k, s in tensor_shapes(top)}
+    return {k: random_tensor(s, gen, device, std, norm_std, k) for k, s in tensor_shapes(top)}
 
 
 def iter_random_state(top, seed=0, std=0.02, norm_std=0.1, device='cuda'):
@@ -67,7 +72,7 @@ def iter_random_state(top, seed=0, std=0.02, norm_std=0.1, device='cuda'):
                 t[r:e] = (torch.randn((e - r, s[1]), generator=gen, device=device) * std).to(torch.bfloat16)
             yield k, t
         else:
-            yield k, random_tensor(s, gen, device, std, norm_std)
+            yield k, random_tensor(s, gen, device, std, norm_std, k)
 
 
 def write_checkpoint(model_dir, top, state):

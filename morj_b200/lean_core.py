@@ -135,23 +135,25 @@ class _Tables:
 
 class LeanGemma4:
     def __init__(self, model_dir, device='cuda', workspace_mb=512, retain_budget_gb=10.0, single_max=16384,
-                 step_tokens=8192):
+                 step_tokens=8192, *, tp_group=None):
         """Load a safetensors checkpoint (`config.json["text_config"]` + `model.language_model.*` tensors) as the
         reference does (`lean_core.py:340-416`). `workspace_mb` is accepted for interface compatibility; the tree
-        attention kernel needs no workspace."""
+        attention kernel needs no workspace. `tp_group`: a torch.distributed process group (NCCL) to shard the model
+        over for tensor parallelism (`morj_b200.tp`); None runs the whole model on this GPU."""
         top, get = open_checkpoint(model_dir, device)
-        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens)
+        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens, tp_group)
 
     @classmethod
-    def from_state(cls, top, state, device='cuda', retain_budget_gb=10.0, single_max=16384, step_tokens=8192):
+    def from_state(cls, top, state, device='cuda', retain_budget_gb=10.0, single_max=16384, step_tokens=8192,
+                   tp_group=None):
         """An engine over an in-memory state dict in the checkpoint's key layout (tensors on any device)."""
         self = cls.__new__(cls)
-        self._setup(top, lambda k: state[k].to(device), device, retain_budget_gb, single_max, step_tokens)
+        self._setup(top, lambda k: state[k].to(device), device, retain_budget_gb, single_max, step_tokens, tp_group)
         return self
 
     @classmethod
     def random_init(cls, top, seed=0, device='cuda', std=0.02, norm_std=0.1, retain_budget_gb=10.0,
-                    single_max=16384, step_tokens=8192):
+                    single_max=16384, step_tokens=8192, tp_group=None):
         """An engine over seeded random-init weights generated on `device` (no checkpoint on disk); tensors are drawn
         in checkpoint order and handed over one at a time, so the peak memory is the model plus one layer."""
         gen = iter_random_state(top, seed=seed, std=std, norm_std=norm_std, device=device)
@@ -163,10 +165,17 @@ class LeanGemma4:
                 cache[k] = t
             return cache.pop(key)
         self = cls.__new__(cls)
-        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens)
+        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens, tp_group)
         return self
 
-    def _setup(self, top, get, device, retain_budget_gb, single_max, step_tokens):
+    def _setup(self, top, get, device, retain_budget_gb, single_max, step_tokens, tp_group=None):
+        self.tp_group, self.tp_world, self.tp_rank = tp_group, 1, 0
+        if tp_group is not None:
+            import torch.distributed as dist
+            from .tp import shard_config, shard_getter
+            self.tp_world, self.tp_rank = dist.get_world_size(tp_group), dist.get_rank(tp_group)
+            get = shard_getter(top, get, self.tp_rank, self.tp_world)
+            top = shard_config(top, self.tp_world)
         cfg = top['text_config']
         self.image_id, self.boi_id, self.eoi_id = (top.get('image_token_id'), top.get('boi_token_id'),
                                                    top.get('eoi_token_id'))
@@ -540,6 +549,20 @@ class LeanGemma4:
         self._k('gemm_geglu' if epi == nat.EPI_GEGLU else 'gemm', 'morj_gemm_bf16', a.data_ptr(), a.stride(0), wp,
                 w.stride(0), out.data_ptr(), out.stride(0), M, N, K, epi, self._stream(), flops=2 * M * N * K)
 
+    def _reduce(self, t):
+        """Tensor parallelism: sum the row-parallel projection's partial output over the ranks (NCCL all-reduce on
+        the current stream); nothing on one GPU."""
+        if self.tp_world > 1:
+            import torch.distributed as dist
+            if self.trace is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                dist.all_reduce(t, group=self.tp_group)
+                e1.record()
+                self.trace.append(('allreduce', 0, e0, e1))
+            else:
+                dist.all_reduce(t, group=self.tp_group)
+
     def _qkv(self, a, layer, row0, M, hq, hk, has_v, d, kind, positions, slots, q_out, k_pool, v_pool):
         """QKV projection with the fused head norm + RoPE + pool scatter (`morj_gemm_qkv_rope`); `row0` skips the q
         rows of the fused weight for the K/V-only call."""
@@ -606,10 +629,12 @@ class LeanGemma4:
             self._attention(q_i, k_pool, v_pool, a_i, t, 'qo', 'kv_indptr_' + kk, 'kv_indices_' + kk, n_seg,
                             nb if kind == 'sliding_attention' else 0, kind, 'work_' + kk, n_work[kk])
             self._gemm(a_i, layer['o'], o)
+            self._reduce(o)
             self._k('rows', 'morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_attn'].data_ptr(),
                      layer['pre_ff'].data_ptr(), n, H, eps, s)
             self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
             self._gemm(act, layer['down'], o)
+            self._reduce(o)
             nxt = self.layers[i + 1]['in_ln'] if i < last else layer['in_ln']
             self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_ff'].data_ptr(),
                      layer['scalar'].data_ptr(), nxt.data_ptr(), n, H, eps, int(i < last), s)
@@ -645,6 +670,7 @@ class LeanGemma4:
                         n_work['ro'])
         o = torch.empty(R, H, dtype=bf, device=dev)
         self._gemm(attn, layer['o'], o)
+        self._reduce(o)
         xr = torch.empty(R, H, dtype=bf, device=dev)
         self._k('rows', 'morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), R, H, xr.data_ptr(), H, s)
         h2 = torch.empty(R, H, dtype=bf, device=dev)
@@ -654,6 +680,7 @@ class LeanGemma4:
         act = torch.empty(R, F, dtype=bf, device=dev)
         self._gemm(h2, layer['gu'], act, nat.EPI_GEGLU)
         self._gemm(act, layer['down'], o)
+        self._reduce(o)
         self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), xr.data_ptr(), xr.data_ptr(), layer['post_ff'].data_ptr(),
                  layer['scalar'].data_ptr(), layer['in_ln'].data_ptr(), R, H, eps, 0, s)
         return xr, rows

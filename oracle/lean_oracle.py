@@ -202,6 +202,8 @@ class OracleModel:
                 pre_ff=g(p + 'pre_feedforward_layernorm.weight'), post_ff=g(p + 'post_feedforward_layernorm.weight'),
                 scalar=g(p + 'layer_scalar').to(BF)))
         self.inv = inv_freqs(cfg)
+        # tensor-parallel check only: sums a row-parallel projection's partial output over ranks (None: one device)
+        self.reduce = None
 
     def embed_rows(self, tokens, feature_rows=None, features=None, bf16=True):
         """embed[tok] * bf16(sqrt(H)) in BF16 (reference `lean_core.py:366,641`), or * sqrt(H) in FP32; image rows
@@ -243,10 +245,14 @@ class OracleModel:
                               nb, window, 1.0)
         attn = _r(attn, bf16).reshape(n, hq * d)
         o = _r(matmul(attn, layer['o'], bf16), bf16)
+        if self.reduce is not None:
+            o = self.reduce(o)
         x, h2 = attn_epilogue(o, x, layer['post_attn'], layer['pre_ff'], eps, bf16)
         gu = _r(matmul(h2, layer['gu'], bf16), bf16)
         act = geglu(gu, bf16)
         dn = _r(matmul(act, layer['down'], bf16), bf16)
+        if self.reduce is not None:
+            dn = self.reduce(dn)
         nxt = self.layers[i + 1]['in_ln'] if i + 1 < len(self.layers) else None
         x, h = mlp_epilogue(dn, x, layer['post_ff'], layer['scalar'], nxt, eps, bf16)
         return x, h, attn

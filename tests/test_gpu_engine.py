@@ -132,3 +132,44 @@ def test_a_pass_too_large_for_the_budget_raises_memory_error(state):
     req = m.prepare(c['seqs'], c['label_ids'])
     with pytest.raises(MemoryError):
         m.run(req, [0, 1, 2, 3], available=1)
+
+
+def full_width_model(vocab=4096):
+    """The 31B-class layer dimensions (hidden 5376, 32 / 16 heads of 128, GeGLU 21504, window 1024) with two layers
+    (one sliding, one global) and a small vocabulary: full-size kernels, an oracle run of seconds."""
+    top = workloads.gemma31b_config()
+    cfg = dict(top['text_config'], layer_types=['sliding_attention', 'full_attention'], num_hidden_layers=2,
+               vocab_size=vocab)
+    top = dict(top, text_config=cfg, image_token_id=vocab - 1, boi_token_id=vocab - 2, eoi_token_id=vocab - 3)
+    state = {k: v.cpu() for k, v in random_state(top, seed=11, device='cuda').items()}
+    return top, state
+
+
+@pytest.mark.parametrize('kind', ['text', 'images'])
+def test_full_width_layers_match_oracle(kind):
+    """Parity at the 31B layer width on the text-tree shape (1500-token prefix, 9 branches of 60), and with two image
+    blocks (560 soft tokens, and 1100 > the 1024 window: the explicit-mask path) in the shared prefix."""
+    if not torch.cuda.is_available():
+        pytest.skip('no CUDA device')
+    from morj_b200.lean_core import LeanGemma4, expand_images
+    from morj_b200.tree import Tree
+    from oracle.lean_oracle import OracleModel
+    top, state = full_width_model()
+    images = None
+    if kind == 'text':
+        t = workloads.text_tree(3, vocab=4096)
+        seqs, labels = t['seqs'], t['label_ids']
+    else:
+        rng = np.random.default_rng(4)
+        img = top['image_token_id']
+        head = [int(v) for v in rng.integers(0, 4000, 20)] + [img] + [int(v) for v in rng.integers(0, 4000, 30)] + [img]
+        seqs = [head + [int(v) for v in rng.integers(0, 4000, n)] for n in (40, 25, 60)]
+        labels = [[5, 6, 7], [5, 6, 7], list(range(100, 355))]
+        g = torch.Generator().manual_seed(5)
+        images = [(torch.randn(n, 5376, generator=g) / 5376 ** 0.5).to(torch.bfloat16) for n in (560, 1100)]
+    m = LeanGemma4.from_state(top, state, device='cuda')
+    req = m.prepare(seqs, labels, images=[f.cuda() for f in images] if images else None)
+    got = flat(m.run(req, list(range(len(seqs)))))
+    oracle = flat(OracleModel(top, state).forward_tree(Tree, seqs, labels, 'bf16', images=images,
+                                                       expand=expand_images))
+    assert np.abs(got - oracle).max() <= TOL, np.abs(got - oracle).max()

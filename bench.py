@@ -279,6 +279,9 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency'])
+    ap.add_argument('--mode', default='replicas', choices=['replicas', 'tp'],
+                    help='replicas: one model per GPU on independent trees (weak scaling); tp: one tree, the model '
+                         'sharded over all GPUs with NCCL all-reduces (strong scaling, single-tree latency)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window'],
                     help='time one kernel alone instead of the tree forward')
@@ -316,12 +319,13 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    tp = args.mode == 'tp' and world > 1
     top = w.gemma31b_config()
     t_init = time.perf_counter()
-    model = LeanGemma4.random_init(top, seed=0, device=dev)
+    model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD if tp else None)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t_init
-    tree_in, desc = workload(args.workload, rank)
+    tree_in, desc = workload(args.workload, 0 if tp else rank)
     images = [f.to(dev) for f in tree_in['images']] if tree_in['images'] else None
     seqs = list(range(len(tree_in['seqs'])))
     req = model.prepare(tree_in['seqs'], tree_in['label_ids'], images=images)
@@ -368,19 +372,21 @@ def main():
         e2e_ms = e2.elapsed_time(e3) / args.steps
         h2d, d2h = model.h2d_bytes, model.d2h_bytes
         # ---- the same planned pass captured once in a CUDA graph and replayed (launch gaps between kernels gone) ----
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            model.execute_pass(prepared)
-        graph.replay()
-        barrier()
-        e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e4.record()
-        for _ in range(args.steps):
+        graph_ms = None
+        if not tp:  # (a graph holding NCCL calls is not worth its teardown rules here)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                model.execute_pass(prepared)
             graph.replay()
-        e5.record()
-        barrier()
-        graph_ms = e4.elapsed_time(e5) / args.steps
-        del graph
+            barrier()
+            e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e4.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e5.record()
+            barrier()
+            graph_ms = round(e4.elapsed_time(e5) / args.steps, 3)
+            del graph
         # ---- one traced step (CUDA events around every kernel) for the per-kernel roofline -----------------------
         model.trace = []
         model.execute_pass(prepared)
@@ -395,8 +401,9 @@ def main():
         d['flops'] += fl
     ms_max = max_over_ranks(ms)
     e2e_max = max_over_ranks(e2e_ms)
-    value = tokens * world / (ms_max / 1000)
-    e2e_value = tokens * world / (e2e_max / 1000)
+    trees = 1 if tp else world  # tensor parallelism: all ranks work on the same tree
+    value = tokens * trees / (ms_max / 1000)
+    e2e_value = tokens * trees / (e2e_max / 1000)
     pk = peaks()
     # dominant kernel: the gate/up GEMM with the GeGLU epilogue (M = tree tokens, N = 2 x 21504, K = 5376); the
     # last layer's readout-only launch (M = reads) is left out so every averaged launch has the captured shape
@@ -411,7 +418,7 @@ def main():
     if os.path.exists(tfile):
         with open(tfile) as f:
             tr = json.load(f)
-        if tr.get('M') == tokens:
+        if tr.get('M') == tokens and not tp:
             traffic = tr.get('bytes_per_launch')
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -426,13 +433,15 @@ def main():
     if rank == 0:
         line = dict(
             metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
-            ms_per_step=ms_max, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
+            ms_per_step=ms_max, higher_is_better=True, scaling='strong' if tp else 'weak', vs_baseline=None,
+            dtype='bf16',
             data='synthetic (seeded random-init weights N(0, 0.02), uniform token ids)',
             config=dict(workload=f'31B-class Gemma-style decoder, {desc}', tokens=tokens,
-                        parallelism=f'replicas x{world} (independent trees, no collective)',
+                        parallelism=(f'tensor parallel x{world} (NCCL all-reduce after O and down)' if tp else
+                                     f'replicas x{world} (independent trees, no collective)'),
                         l2='inputs larger than L2 (52 GB of weights streamed per step)',
                         tflops_per_tree_specified=round((flops_lin + flops_attn) / 1e12, 2)),
-            model_tflops=round((flops_lin + flops_attn) / (ms_max / 1000) / 1e12, 1),
+            model_tflops=round(trees * (flops_lin + flops_attn) / (ms_max / 1000) / 1e12, 1),
             p50_tree_latency_ms=round(statistics.median(lat), 3),
             roofline=dict(bound='tensor', kernel=f'gemm_kernel<GEGLU> gate/up projection {tokens}x43008x5376',
                           achieved=round(achieved, 1), peak=pk['bf16_sustained'], unit='TFLOP/s',
@@ -441,7 +450,7 @@ def main():
                           launches=len(big), avg_launch_us=round(1000 * g_ms / max(len(big), 1), 2),
                           all_gemms_tflops=round(all_tf, 1)),
             breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
-            traced_span_ms=round(trace_span, 3), graph_replay_ms=round(graph_ms, 3),
+            traced_span_ms=round(trace_span, 3), graph_replay_ms=graph_ms,
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
                      ms_per_step=e2e_max),
             gpu_launches=int(launches * args.steps),

@@ -49,6 +49,10 @@ def workload(name, rank):
     if name == 'multimodal':
         return (w.multimodal_tree(seed=rank),
                 'multimodal tree: 8 x 560 image soft tokens + 300 text + 2 questions x 4 rotations x 40 tokens')
+    if name == 'sweep':
+        forests = w.pack_forests(w.sweep_trees(seed=rank, count=64))
+        return forests, (f'replication sweep: 64 seeded trees per GPU (prefix log-uniform 64-8192, 2-8 branches of '
+                         f'16-128, 2-16 labels) packed into {len(forests)} forests of <= 8192 tokens')
     raise ValueError(name)
 
 
@@ -278,7 +282,7 @@ def main():
     ap.add_argument('--steps', type=int, default=10)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency'])
+    ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency', 'sweep'])
     ap.add_argument('--mode', default='replicas', choices=['replicas', 'tp'],
                     help='replicas: one model per GPU on independent trees (weak scaling); tp: one tree, the model '
                          'sharded over all GPUs with NCCL all-reduces (strong scaling, single-tree latency)')
@@ -326,22 +330,33 @@ def main():
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t_init
     tree_in, desc = workload(args.workload, 0 if tp else rank)
-    images = [f.to(dev) for f in tree_in['images']] if tree_in['images'] else None
-    seqs = list(range(len(tree_in['seqs'])))
-    req = model.prepare(tree_in['seqs'], tree_in['label_ids'], images=images)
-    prepared = model.prepare_pass(req, seqs)
-    tokens = prepared['tokens']
-    flops_lin = w.linear_flops_per_token(top) * tokens
-    pairs = w.attention_pairs(prepared['plan'], top['text_config']['sliding_window'], top['text_config']['layer_types'])
+    requests = tree_in if isinstance(tree_in, list) else [tree_in]
+    reqs, preps = [], []
+    for r in requests:
+        images = [f.to(dev) for f in r['images']] if r['images'] else None
+        req = model.prepare(r['seqs'], r['label_ids'], images=images)
+        reqs.append((req, list(range(len(r['seqs'])))))
+        preps.append(model.prepare_pass(req, list(range(len(r['seqs'])))))
+    tokens = sum(p['tokens'] for p in preps)
     c = top['text_config']
+    flops_lin = w.linear_flops_per_token(top) * tokens
+    pairs = sum(w.attention_pairs(p['plan'], c['sliding_window'], c['layer_types']) for p in preps)
     flops_attn = 4 * c['num_attention_heads'] * c['head_dim'] * pairs
+
+    def execute_all():
+        for p in preps:
+            model.execute_pass(p)
+
+    def run_all():
+        for req, seqs in reqs:
+            model.run(req, seqs)
     props = torch.cuda.get_device_properties(dev)
     clocks = Clocks('GPU-' + str(props.uuid) if hasattr(props, 'uuid') else str(local))
 
     # ---- device-timed forward over a resident plan -------------------------------------------------------------
     with torch.inference_mode():
         for _ in range(args.warmup):
-            model.execute_pass(prepared)
+            execute_all()
         barrier()
         clocks.start()
         launches0 = model.launches
@@ -349,14 +364,14 @@ def main():
         barrier()
         e0.record()
         for _ in range(args.steps):
-            model.execute_pass(prepared)
+            execute_all()
         e1.record()
         barrier()
         ms = e0.elapsed_time(e1) / args.steps
         launches = (model.launches - launches0) // args.steps
         # ---- end to end through the public call (host ids -> host probabilities) --------------------------------
         for _ in range(2):
-            model.run(req, seqs)
+            run_all()
         barrier()
         lat = []
         e2 = torch.cuda.Event(enable_timing=True)
@@ -364,19 +379,20 @@ def main():
         e2.record()
         for _ in range(args.steps):
             t0 = time.perf_counter()
-            model.run(req, seqs)
+            run_all()
             lat.append(1000 * (time.perf_counter() - t0))
         e3.record()
         barrier()
         clocks.stop()
         e2e_ms = e2.elapsed_time(e3) / args.steps
-        h2d, d2h = model.h2d_bytes, model.d2h_bytes
+        h2d = sum(p['h2d_bytes'] for p in preps) if len(preps) > 1 else model.h2d_bytes
+        d2h = 4 * sum(p['ro']['n_labels'] for p in preps)
         # ---- the same planned pass captured once in a CUDA graph and replayed (launch gaps between kernels gone) ----
         graph_ms = None
         if not tp:  # (a graph holding NCCL calls is not worth its teardown rules here)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                model.execute_pass(prepared)
+                execute_all()
             graph.replay()
             barrier()
             e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -389,7 +405,7 @@ def main():
             del graph
         # ---- one traced step (CUDA events around every kernel) for the per-kernel roofline -----------------------
         model.trace = []
-        model.execute_pass(prepared)
+        execute_all()
         torch.cuda.synchronize()
         trace, model.trace = model.trace, None
         trace_span = trace[0][2].elapsed_time(trace[-1][3])
@@ -418,7 +434,7 @@ def main():
     if os.path.exists(tfile):
         with open(tfile) as f:
             tr = json.load(f)
-        if tr.get('M') == tokens and not tp:
+        if tr.get('M') == tokens and not tp and len(preps) == 1:
             traffic = tr.get('bytes_per_launch')
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

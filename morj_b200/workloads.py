@@ -124,6 +124,25 @@ def sweep_trees(seed=0, count=64, vocab=262144):
     return out
 
 
+def pack_forests(trees, budget=8192):
+    """Greedy packing of independent trees (in order) into forests of at most `budget` distinct tokens (a tree
+    larger than the budget is a forest of its own). A forest is one request: its trees share no prefix, so the planner
+    lays them out as separate roots and one forward computes them all."""
+    from .tree import Tree
+    forests, cur, used = [], [], 0
+    for t in trees:
+        n = Tree(t['seqs']).num_tokens
+        if cur and used + n > budget:
+            forests.append(cur)
+            cur, used = [], 0
+        cur.append(t)
+        used += n
+    if cur:
+        forests.append(cur)
+    return [dict(seqs=[s for t in f for s in t['seqs']], label_ids=[l for t in f for l in t['label_ids']],
+                 images=None, trees=len(f)) for f in forests]
+
+
 def linear_flops_per_token(top):
     """2 x linear parameters over all layers (QKV, O, gate/up, down): FLOPs per computed token."""
     c = top['text_config']

@@ -229,8 +229,8 @@ def kernel_arm(args):
         M, N, K = args.m, args.n, args.k
         a = torch.randn(M, K, device=dev).to(torch.bfloat16)
         b = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
-        epi = nat.EPI_GEGLU if args.kernel == 'geglu' else nat.EPI_STORE
-        c = torch.empty(M, N // 2 if epi else N, device=dev, dtype=torch.bfloat16)
+        epi = (nat.EPI_GEGLU if args.kernel == 'geglu' else nat.EPI_STORE) | args.force
+        c = torch.empty(M, N // 2 if args.kernel == 'geglu' else N, device=dev, dtype=torch.bfloat16)
         flops = 2 * M * N * K
 
         def launch():
@@ -289,6 +289,8 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window'],
                     help='time one kernel alone instead of the tree forward')
+    ap.add_argument('--force', type=lambda v: int(v, 0), default=0,
+                    help='kernel mode: or-ed into the GEMM epilogue (0x100 SM-pair kernel, 0x200 one-CTA kernel)')
     ap.add_argument('--m', type=int, default=2040)
     ap.add_argument('--n', type=int, default=43008)
     ap.add_argument('--k', type=int, default=5376)

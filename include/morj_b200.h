@@ -43,6 +43,10 @@ extern "C" {
 #define MORJ_EPI_GEGLU 1 /* B rows interleaved in 128-row blocks (gate block, up block, ...); C[M,N/2] =
                             bf16(gelu_tanh(bf16(gate)) * bf16(up)) */
 #define MORJ_EPI_QKV_D128 2 /* internal: the fused QKV epilogue of morj_gemm_qkv_rope, 128-wide heads */
+/* Kernel choice, or-ed into morj_gemm_bf16's epilogue argument (default: chosen per shape): the one-CTA kernel
+ * (128-row tiles) or the SM-pair kernel (256-row tiles, tcgen05.mma.cta_group::2 over a 2-CTA cluster). */
+#define MORJ_GEMM_FORCE_PAIR 0x100
+#define MORJ_GEMM_FORCE_SINGLE 0x200
 #define MORJ_EPI_QKV_D64 3  /* internal: the same, 64-wide heads */
 
 /* Library version (major * 10000 + minor * 100 + patch). */

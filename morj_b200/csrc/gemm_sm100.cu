@@ -381,6 +381,189 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Pair kernel: a cluster of two CTAs on two SMs computes a 256 x BN tile with tcgen05.mma.cta_group::2. CTA r loads
+// A rows [128 r, 128 r + 128) of the tile and B rows [r BN / 2, (r + 1) BN / 2); the MMA issued by CTA 0 reads both
+// CTAs' shared memory and leaves rows [128 r, 128 r + 128) of the accumulator in CTA r's TMEM. Each SM fills only
+// half of the B tile per k-block, so the L2-to-shared-memory traffic per FLOP drops by a third against the one-CTA
+// kernel. The epilogues are the one-CTA kernel's (each CTA drains its own 128 rows).
+// ---------------------------------------------------------------------------------------------------------------
+template <int BN>
+struct Cfg2 {
+  static_assert(BN % 32 == 0 || BN % 16 == 0, "tile width");
+  static constexpr int B_HALF_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_HALF_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN);
+};
+
+template <int EPI, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe) {
+  using C_ = Cfg2<BN>;
+  constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars: full[STAGES] (used in CTA 0), empty[STAGES], acc_full[2], acc_empty[2] (used in CTA 0), done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
+  const uint32_t done0 = smem_u32(bars + 2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 8);  // one arrival per epilogue warp of each CTA of the pair
+    }
+    mbar_init(done0, 1);
+    *abort = 0;
+    fence_mbar_init();
+    tma_prefetch(&map_a);
+    tma_prefetch(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs are initialised before either CTA signals the other's
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (M + 2 * BM - 1) / (2 * BM), num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + BK - 1) / BK;
+  const uint32_t smem_base = smem_u32(smem);
+  const int cluster = blockIdx.x / 2, n_clusters = gridDim.x / 2;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // this CTA's loads complete on CTA 0's full barriers; CTA 0 posts the byte count of both CTAs
+      const uint32_t full0_leader = map_shared(full0, 0);
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_normal();
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int t = cluster; t < tiles && !*abort; t += n_clusters) {
+        const TileCoord tc = tile_coord(t, num_m, num_n);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kErrTimeoutGemmProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_base + stage * STAGE_BYTES;
+          if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * stage, 2 * STAGE_BYTES);
+          tma_load_2d_pair(sa, &map_a, full0_leader + 8 * stage, kb * BK, tc.m * 2 * BM + rank * BM, pol_a);
+          tma_load_2d_pair(sa + A_BYTES, &map_b, full0_leader + 8 * stage, kb * BK,
+                           tc.n * BN + rank * (BN / 2), pol_b);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // no copy of this CTA may still be in flight when it leaves: its last fills are consumed (empty) first
+      const int pending = issued < STAGES ? issued : STAGES;
+      for (int j = 0; j < pending; ++j) {
+        if (!mbar_wait_landed(empty0 + 8 * stage, phase ^ 1)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = cluster; t < tiles; t += n_clusters) {
+        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kErrTimeoutGemmMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 256;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, abort, kErrTimeoutGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16_pair(d_tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), C_::IDESC, (kb | k) != 0);
+          }
+          umma_commit_pair(empty0 + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(accf0 + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit_pair(done0);
+      mbar_wait_landed(done0, 0);
+    }
+  } else {
+    // epilogue warps 2..5 of each CTA drain that CTA's 128 accumulator rows
+    const int quarter = warp & 3;
+    const uint32_t acce_leader = map_shared(acce0, 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster; t < tiles; t += n_clusters) {
+      const TileCoord tc = tile_coord(t, num_m, num_n);
+      int ok = lane == 0 ? (int)mbar_wait(accf0 + 8 * acc, acc_phase, abort, kErrTimeoutGemmEpilogue) : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = tc.m * 2 * BM + rank * BM + quarter * 32 + lane;
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
+      if constexpr (EPI == MORJ_EPI_QKV_D128) {
+        epilogue_qkv<BN, 128>(tacc, row, tc.n, row < M, qe, N);
+      } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
+        epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
+      } else {
+        epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_leader + 8 * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs or the peer's signals may still touch it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -464,26 +647,57 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
   return check_launch("gemm_kernel");
 }
 
-// Tile width: the smallest (waves x per-tile time) over the candidates, where a wave is one tile per SM and a tile's
-// time per 64-deep k-block is the larger of its MMA time (2 x BN cycles for M = 128) and the time to fill its A and B
-// stage from L2 (about 1.28 cycles per 128-byte row, 128 + BN rows); ties go to the wider tile.
-static int pick_bn(int M, int N, const int* cand = nullptr, int n_cand = 0) {
-  static const int all[] = {256, 240, 224, 208, 192, 176, 160, 128};
-  if (!cand) {
-    cand = all;
-    n_cand = 8;
+template <int EPI, int BN>
+static int launch2(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
+                   int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}) {
+  using C_ = Cfg2<BN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C_::SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = true;
   }
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, A, M, K, lda, BM);
+  if (st) return st;
+  st = make_map(&mb, B, N, K, ldb, BN / 2);
+  if (st) return st;
+  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+  const int pairs = num_sms() / 2;
+  const int clusters = tiles < pairs ? tiles : pairs;
+  gemm2_kernel<EPI, BN><<<2 * clusters, THREADS, C_::SMEM_BYTES, stream>>>(
+      ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe);
+  return check_launch("gemm2_kernel");
+}
+
+// Kernel and tile width: the smallest (waves x per-tile time) over the candidates. A wave is one tile per SM (one
+// 256-row tile per SM pair for the pair kernel); a tile's time per 64-deep k-block is the larger of its MMA time
+// (2 x BN cycles) and the time to fill its stage from L2 (about 1.46 cycles per 128-byte row, measured on the 31B
+// shapes: 128 + BN rows for one CTA, 128 + BN / 2 per SM for the pair). Ties go to the pair kernel, then to the wider
+// tile.
+struct Choice {
+  int bn;
+  bool pair;
+};
+static Choice pick(int M, int N, const int* cand, int n_cand, int force) {
   const int sms = num_sms();
-  int best = cand[0];
+  Choice best{cand[0], false};
   double best_cost = -1;
-  for (int i = 0; i < n_cand; ++i) {
-    const int bn = cand[i];
-    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-    const double per_tile = 2.0 * bn > 1.28 * (BM + bn) ? 2.0 * bn : 1.28 * (BM + bn);
-    const double cost = (double)((tiles + sms - 1) / sms) * per_tile;
-    if (best_cost < 0 || cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = bn;
+  for (int p = 1; p >= 0; --p) {
+    if ((force == 1 && p == 0) || (force == 2 && p == 1)) continue;
+    for (int i = 0; i < n_cand; ++i) {
+      const int bn = cand[i];
+      const long long rows = p ? (M + 2 * BM - 1) / (2 * BM) : (M + BM - 1) / BM;
+      const long long tiles = rows * ((N + bn - 1) / bn);
+      const int slots = p ? sms / 2 : sms;
+      const double fill = 1.46 * (BM + (p ? bn / 2 : bn));
+      const double per_tile = 2.0 * bn > fill ? 2.0 * bn : fill;
+      const double cost = (double)((tiles + slots - 1) / slots) * per_tile;
+      if (best_cost < 0 || cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = Choice{bn, p == 1};
+      }
     }
   }
   return best;
@@ -503,22 +717,36 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int force = (epilogue & MORJ_GEMM_FORCE_PAIR) ? 1 : (epilogue & MORJ_GEMM_FORCE_SINGLE) ? 2 : 0;
+  epilogue &= 0xff;
   if (epilogue == MORJ_EPI_STORE) {
     if (N % 16 || ldc < N) return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: N must be a multiple of 16 (N=%d)", N);
-    switch (gemm::pick_bn(M, N)) {
-      case 240: return gemm::launch<MORJ_EPI_STORE, 240>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      case 224: return gemm::launch<MORJ_EPI_STORE, 224>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      case 208: return gemm::launch<MORJ_EPI_STORE, 208>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      case 192: return gemm::launch<MORJ_EPI_STORE, 192>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      case 176: return gemm::launch<MORJ_EPI_STORE, 176>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      case 160: return gemm::launch<MORJ_EPI_STORE, 160>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      case 128: return gemm::launch<MORJ_EPI_STORE, 128>(A, lda, B, ldb, C, ldc, M, N, K, s);
-      default: return gemm::launch<MORJ_EPI_STORE, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
+    static const int cand[] = {256, 240, 224, 208, 192, 176, 160, 128};
+    const gemm::Choice c = gemm::pick(M, N, cand, 8, force);
+#define MORJ_STORE_CASE(W)                                                                   \
+  case W:                                                                                    \
+    return c.pair ? gemm::launch2<MORJ_EPI_STORE, W>(A, lda, B, ldb, C, ldc, M, N, K, s)     \
+                  : gemm::launch<MORJ_EPI_STORE, W>(A, lda, B, ldb, C, ldc, M, N, K, s);
+    switch (c.bn) {
+      MORJ_STORE_CASE(240)
+      MORJ_STORE_CASE(224)
+      MORJ_STORE_CASE(208)
+      MORJ_STORE_CASE(192)
+      MORJ_STORE_CASE(176)
+      MORJ_STORE_CASE(160)
+      MORJ_STORE_CASE(128)
+      default:
+        return c.pair ? gemm::launch2<MORJ_EPI_STORE, 256>(A, lda, B, ldb, C, ldc, M, N, K, s)
+                      : gemm::launch<MORJ_EPI_STORE, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
     }
+#undef MORJ_STORE_CASE
   }
   if (epilogue == MORJ_EPI_GEGLU) {
     if (N % 256 || ldc < N / 2)
       return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: GEGLU needs N a multiple of 256 (N=%d)", N);
+    static const int cand[] = {256};
+    if (gemm::pick(M, N, cand, 1, force).pair)
+      return gemm::launch2<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
     return gemm::launch<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
   }
   return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: unknown epilogue %d", epilogue);
@@ -542,15 +770,20 @@ extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, l
                  inv_freq, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool, (__nv_bfloat16*)v_pool};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   static const int cand[] = {256, 128};
+  const gemm::Choice c = gemm::pick(M, N, cand, 2, 0);
   if (d == 128) {
-    if (gemm::pick_bn(M, N, cand, 2) == 128)
-      return gemm::launch<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
-    return gemm::launch<MORJ_EPI_QKV_D128, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+    if (c.bn == 128)
+      return c.pair ? gemm::launch2<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)
+                    : gemm::launch<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+    return c.pair ? gemm::launch2<MORJ_EPI_QKV_D128, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)
+                  : gemm::launch<MORJ_EPI_QKV_D128, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
   }
   if (d == 64) {
-    if (gemm::pick_bn(M, N, cand, 2) == 128)
-      return gemm::launch<MORJ_EPI_QKV_D64, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
-    return gemm::launch<MORJ_EPI_QKV_D64, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+    if (c.bn == 128)
+      return c.pair ? gemm::launch2<MORJ_EPI_QKV_D64, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)
+                    : gemm::launch<MORJ_EPI_QKV_D64, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
+    return c.pair ? gemm::launch2<MORJ_EPI_QKV_D64, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)
+                  : gemm::launch<MORJ_EPI_QKV_D64, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
   }
   return set_error(MORJ_ERR_UNSUPPORTED, "morj_gemm_qkv_rope: head_dim %d unsupported (64, 128)", d);
 }

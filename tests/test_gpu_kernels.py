@@ -341,3 +341,36 @@ def test_fused_qkv_gemm_matches_gemm_then_oracle_head_epilogue(M, H, d, hq, hk, 
     if hk:
         close(kp[torch.as_tensor(slots)], k)
         close(vp[torch.as_tensor(slots)], v)
+
+
+@pytest.mark.parametrize('force', [0x100, 0x200])
+@pytest.mark.parametrize('M,N,K', [(1, 16, 64), (130, 272, 200), (256, 256, 128), (300, 5376, 512),
+                                   (2040, 8192, 576), (2040, 5376, 640), (517, 2048, 1024)])
+def test_gemm_pair_and_single_kernels(force, M, N, K):
+    """The SM-pair kernel (tcgen05.mma.cta_group::2, 2-CTA clusters) and the one-CTA kernel on the same shapes."""
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    c = torch.full((M, N), float('nan'), device=DEV, dtype=torch.bfloat16)
+    nat.call('morj_gemm_bf16', a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), N, M, N, K,
+             nat.EPI_STORE | force, stream())
+    torch.cuda.synchronize()
+    close(c, a.float() @ b.float().T)
+
+
+@pytest.mark.parametrize('force', [0x100, 0x200])
+def test_gemm_geglu_pair_and_single(force):
+    from morj_b200.lean_core import interleave_glu
+    from oracle.lean_oracle import gelu_tanh
+    M, F, K = 700, 1024, 512
+    a = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    gate = (torch.randn(F, K, device=DEV) * 0.05).to(torch.bfloat16)
+    up = (torch.randn(F, K, device=DEV) * 0.05).to(torch.bfloat16)
+    w = interleave_glu(gate, up).contiguous()
+    out = torch.empty(M, F, device=DEV, dtype=torch.bfloat16)
+    nat.call('morj_gemm_bf16', a.data_ptr(), K, w.data_ptr(), K, out.data_ptr(), F, M, 2 * F, K,
+             nat.EPI_GEGLU | force, stream())
+    torch.cuda.synchronize()
+    g = (a.float() @ gate.float().T).bfloat16().float()
+    u = (a.float() @ up.float().T).bfloat16().float()
+    close(out, gelu_tanh(g) * u)

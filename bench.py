@@ -214,6 +214,8 @@ def kernel_arm(args):
         qn = torch.ones(d, device=dev, dtype=torch.bfloat16)
         pos = torch.arange(M, device=dev, dtype=torch.int32)
         inv = (1.0 / (10000 ** (torch.arange(0, d, 2, device=dev).float() / d))).contiguous()
+        rope = torch.empty(M, d // 2, 2, device=dev)
+        nat.call('morj_rope_table', inv.data_ptr(), d // 2, M, rope.data_ptr(), s)
         slots = torch.randperm(M, device=dev).to(torch.int32)
         q_out = torch.empty(M, hq, d, device=dev, dtype=torch.bfloat16)
         kp = torch.empty(M, hk, d, device=dev, dtype=torch.bfloat16)
@@ -221,8 +223,9 @@ def kernel_arm(args):
         flops = 2 * M * n_out * H
 
         def launch():
-            nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, 1, d, qn.data_ptr(),
-                     qn.data_ptr(), pos.data_ptr(), inv.data_ptr(), slots.data_ptr(), 1e-6, q_out.data_ptr(),
+            nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, 1 | args.force, d,
+                     qn.data_ptr(),
+                     qn.data_ptr(), pos.data_ptr(), rope.data_ptr(), M, slots.data_ptr(), 1e-6, q_out.data_ptr(),
                      kp.data_ptr(), vp.data_ptr(), s)
         shape = dict(M=M, N=n_out, K=H)
     elif args.kernel in ('gemm', 'geglu'):
@@ -431,11 +434,12 @@ def main():
     achieved = sum(f for f, _ in big) / (g_ms / 1000) / 1e12
     allg = [(fl, a.elapsed_time(b)) for kind, fl, a, b in trace if kind.startswith('gemm')]
     all_tf = sum(f for f, _ in allg) / (sum(t for _, t in allg) / 1000) / 1e12
-    traffic = None
+    traffic, kname = None, 'gemm kernel<GEGLU>'
     tfile = os.path.join(ROOT, 'profiles', 'gemm_geglu_traffic.json')
     if os.path.exists(tfile):
         with open(tfile) as f:
             tr = json.load(f)
+        kname = tr.get('kernel', kname)
         if tr.get('M') == tokens and not tp and len(preps) == 1:
             traffic = tr.get('bytes_per_launch')
     cpu = None
@@ -461,7 +465,7 @@ def main():
                         tflops_per_tree_specified=round((flops_lin + flops_attn) / 1e12, 2)),
             model_tflops=round(trees * (flops_lin + flops_attn) / (ms_max / 1000) / 1e12, 1),
             p50_tree_latency_ms=round(statistics.median(lat), 3),
-            roofline=dict(bound='tensor', kernel=f'gemm_kernel<GEGLU> gate/up projection {tokens}x43008x5376',
+            roofline=dict(bound='tensor', kernel=f'{kname}: gate/up projection {tokens}x43008x5376',
                           achieved=round(achieved, 1), peak=pk['bf16_sustained'], unit='TFLOP/s',
                           frac=round(achieved / pk['bf16_sustained'], 4), traffic=traffic,
                           peak_source=f"{pk['source']} sustained cuBLAS BF16 (kernel timed inside a long step)",

@@ -10,6 +10,7 @@
  *   morj_gemm_bf16            torch.matmul (cuBLAS) at lean_core.py:670,682,685,686,701,708,729,733
  *   morj_gemm_bf16 (GEGLU)    the gate-up matmul + flashinfer.activation.gelu_tanh_and_mul, lean_core.py:685,733
  *   morj_gemm_qkv_rope        the QKV matmul + Triton _qkv_post, lean_core.py:670-674, 701-704, 708-712
+ *   morj_rope_table           the per-step RoPE cos / sin tables, lean_core.py:636-640 (kept per model, by position)
  *   morj_embed_rmsnorm        embedding gather * embed_scale + image feature rows + flashinfer.rmsnorm,
  *                             lean_core.py:641-653
  *   morj_qkv_post             Triton _qkv_post, lean_core.py:234-277 (launches 672-674, 702-704, 710-712) with the
@@ -43,8 +44,9 @@ extern "C" {
 #define MORJ_EPI_GEGLU 1 /* B rows interleaved in 128-row blocks (gate block, up block, ...); C[M,N/2] =
                             bf16(gelu_tanh(bf16(gate)) * bf16(up)) */
 #define MORJ_EPI_QKV_D128 2 /* internal: the fused QKV epilogue of morj_gemm_qkv_rope, 128-wide heads */
-/* Kernel choice, or-ed into morj_gemm_bf16's epilogue argument (default: chosen per shape): the one-CTA kernel
- * (128-row tiles) or the SM-pair kernel (256-row tiles, tcgen05.mma.cta_group::2 over a 2-CTA cluster). */
+/* Kernel choice, or-ed into morj_gemm_bf16's epilogue argument or morj_gemm_qkv_rope's has_v argument (default:
+ * chosen per shape): the one-CTA kernel (128-row tiles) or the SM-pair kernel (256-row tiles,
+ * tcgen05.mma.cta_group::2 over a 2-CTA cluster). */
 #define MORJ_GEMM_FORCE_PAIR 0x100
 #define MORJ_GEMM_FORCE_SINGLE 0x200
 #define MORJ_EPI_QKV_D64 3  /* internal: the same, 64-wide heads */
@@ -70,11 +72,19 @@ int morj_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, v
  * v unweighted), rounded, RoPE'd (q, k) and written straight to q_out[row, hq, d] and pool row slots[row] of
  * k_pool / v_pool. has_v = 0 (full-attention layers): V = the unweighted norm of the K projection. hq = 0 or hk = 0
  * give the K/V-only and q-only calls. Equivalent to morj_gemm_bf16 followed by morj_qkv_post, without the
- * intermediate [M, N] tensor. d in {64, 128}. */
+ * intermediate [M, N] tensor. d in {64, 128}. has_v may carry MORJ_GEMM_FORCE_PAIR / MORJ_GEMM_FORCE_SINGLE.
+ * rope: the RoPE table of morj_rope_table (rope_rows positions x d/2 (cos, sin) FP32 pairs), read at row
+ * positions[row]; a position outside [0, rope_rows) sets the device error word (MORJ device code 0x301) and the row
+ * is not written. rope, q_norm and k_norm 16-byte aligned. */
 int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, long long ldw, int M, int K, int hq, int hk,
                        int has_v, int d, const void* q_norm, const void* k_norm, const int* positions,
-                       const float* inv_freq, const int* slots, float eps, void* q_out, void* k_pool, void* v_pool,
-                       void* stream);
+                       const void* rope, int rope_rows, const int* slots, float eps, void* q_out, void* k_pool,
+                       void* v_pool, void* stream);
+
+/* RoPE table by position (the reference's per-step cos / sin tables, lean_core.py:636-640, built once per model
+ * and grown with the longest position seen): table[p][i] = (cos, sin)(p * inv_freq[i]) as FP32 pairs for
+ * p < rows, i < half (half even). table 16-byte aligned, rows * half * 8 bytes. */
+int morj_rope_table(const float* inv_freq, int half, int rows, void* table, void* stream);
 
 /* Per row i < n: x[i] = bf16(embed[tokens[i]] * scale), or the feature row features[feature_row[i]] when
  * feature_row != NULL and feature_row[i] >= 0; then h[i] = bf16(rmsnorm(x[i]) * norm_w) (FP32 math). H % 8 == 0. */

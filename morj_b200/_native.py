@@ -28,7 +28,8 @@ SIGNATURES = {
     'morj_version': [],
     'morj_device_error': [IP, I, P],
     'morj_gemm_bf16': [P, LL, P, LL, P, LL, I, I, I, I, P],
-    'morj_gemm_qkv_rope': [P, LL, P, LL, I, I, I, I, I, I, P, P, P, P, P, F, P, P, P, P],
+    'morj_gemm_qkv_rope': [P, LL, P, LL, I, I, I, I, I, I, P, P, P, P, I, P, F, P, P, P, P],
+    'morj_rope_table': [P, I, I, P, P],
     'morj_embed_rmsnorm': [P, P, P, P, I, I, F, P, F, P, P, P],
     'morj_qkv_post': [P, LL, I, I, I, I, I, P, P, P, P, P, F, P, P, P, P],
     'morj_tree_attention_work': [IP, IP, IP, I, I, I, I, I, I, IP, I],

@@ -293,6 +293,10 @@ MORJ_DEV float2 unpack_bf16x2(uint32_t v) {
   __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(b);
 }
+MORJ_DEV void unpack8_bf16(uint4 u, float (&v)[8]) {
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y, v[4] = c.x, v[5] = c.y, v[6] = d.x, v[7] = d.y;
+}
 
 // tanh-approximated GELU from its definition 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
 MORJ_DEV float gelu_tanh(float x) {

@@ -45,7 +45,8 @@ struct QkvEpi {
   const __nv_bfloat16* q_norm;
   const __nv_bfloat16* k_norm;
   const int* positions;
-  const float* inv_freq;
+  const float4* rope;  // RoPE table by position: D / 2 (cos, sin) pairs per position
+  int rope_rows;
   const int* slots;
   float eps;
   __nv_bfloat16* q_out;
@@ -68,9 +69,16 @@ MORJ_DEV void store32_bf16(__nv_bfloat16* dst, const float (&v)[32]) {
 // One 128-row tile of the QKV projection, D-wide heads: thread = token row (reference `_qkv_post` numerics).
 template <int BN, int D>
 MORJ_DEV void epilogue_qkv(uint32_t tacc, int row, int n_blk, bool row_ok, const QkvEpi& e, int N) {
+  // the norm weights and the (cos, sin) pairs are read 8 weights / 2 pairs per load
   constexpr int HALF = D / 2;
   const int n_heads = N / D;
-  const float pos = row_ok ? (float)e.positions[row] : 0.f;
+  int pos = row_ok ? e.positions[row] : 0;
+  if ((unsigned)pos >= (unsigned)e.rope_rows) {
+    if (row_ok) report(kErrBadIndex);
+    row_ok = false;
+    pos = 0;
+  }
+  const float4* rope = e.rope + (size_t)pos * (HALF / 2);
   const size_t slot = (row_ok && e.hk) ? (size_t)e.slots[row] : 0;
 #pragma unroll 1
   for (int hh = 0; hh < BN / D; ++hh) {
@@ -112,15 +120,25 @@ MORJ_DEV void epilogue_qkv(uint32_t tacc, int row, int n_blk, bool row_ok, const
       float o1[32], o2[32];
       if (is_q || is_k) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = bf16_round(__uint_as_float(r1[i])) * inv;
-          const float b = bf16_round(__uint_as_float(r2[i])) * inv;
-          const float y1 = bf16_round(a * __bfloat162float(w[c + i]));  // rounded before RoPE, as the reference
-          const float y2 = bf16_round(b * __bfloat162float(w[HALF + c + i]));
-          float sn, cs;
-          sincosf(pos * e.inv_freq[c + i], &sn, &cs);
-          o1[i] = y1 * cs - y2 * sn;
-          o2[i] = y2 * cs + y1 * sn;
+        for (int j = 0; j < 32; j += 8) {
+          float w1[8], w2[8];
+          unpack8_bf16(*reinterpret_cast<const uint4*>(w + c + j), w1);
+          unpack8_bf16(*reinterpret_cast<const uint4*>(w + HALF + c + j), w2);
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            const float4 cs = rope[(c + j + u) / 2];  // (cos, sin) of pairs c+j+u and c+j+u+1
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+              const int i = j + u + v;
+              const float co = v ? cs.z : cs.x, sn = v ? cs.w : cs.y;
+              const float a = bf16_round(__uint_as_float(r1[i])) * inv;
+              const float b = bf16_round(__uint_as_float(r2[i])) * inv;
+              const float y1 = bf16_round(a * w1[u + v]);  // rounded before RoPE, as the reference
+              const float y2 = bf16_round(b * w2[u + v]);
+              o1[i] = y1 * co - y2 * sn;
+              o2[i] = y2 * co + y1 * sn;
+            }
+          }
         }
         if (row_ok) {
           store32_bf16(dst + c, o1);
@@ -754,23 +772,31 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
 
 extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, long long ldw, int M, int K, int hq,
                                   int hk, int has_v, int d, const void* q_norm, const void* k_norm,
-                                  const int* positions, const float* inv_freq, const int* slots, float eps,
+                                  const int* positions, const void* rope, int rope_rows, const int* slots, float eps,
                                   void* q_out, void* k_pool, void* v_pool, void* stream) {
   using namespace morj;
   if (M == 0 || hq + hk == 0) return MORJ_OK;
-  if (!A || !W || !positions || !inv_freq || M < 0 || K <= 0 || hq < 0 || hk < 0 || (hq && (!q_out || !q_norm)) ||
-      (hk && (!k_pool || !v_pool || !slots || !k_norm)))
+  if (!A || !W || !positions || !rope || rope_rows <= 0 || M < 0 || K <= 0 || hq < 0 || hk < 0 ||
+      (hq && (!q_out || !q_norm)) || (hk && (!k_pool || !v_pool || !slots || !k_norm)))
     return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: bad pointers or sizes");
+  if ((reinterpret_cast<uintptr_t>(rope) | reinterpret_cast<uintptr_t>(q_norm) |
+       reinterpret_cast<uintptr_t>(k_norm)) & 15)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: rope table and norm weights must be 16-byte aligned");
   if (K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K)
     return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: K and leading dimensions must be multiples of 8");
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) & 15)
     return set_error(MORJ_ERR_ARG, "morj_gemm_qkv_rope: pointers must be 16-byte aligned");
+  const int force = (has_v & MORJ_GEMM_FORCE_PAIR) ? 1 : (has_v & MORJ_GEMM_FORCE_SINGLE) ? 2 : 0;
+  has_v &= 0xff;
   const int N = (hq + (has_v ? 2 : 1) * hk) * d;
   gemm::QkvEpi e{hq, hk, has_v ? 1 : 0, (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, positions,
-                 inv_freq, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool, (__nv_bfloat16*)v_pool};
+                 (const float4*)rope, rope_rows, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool,
+                 (__nv_bfloat16*)v_pool};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // One-CTA kernel unless forced: with the head epilogue (RMSNorm + sincos RoPE per element, one epilogue warp per
+  // scheduler) the pair kernel measured slower (2040 x 8192 x 5376: 0.192 ms pair, 0.158 ms one-CTA).
   static const int cand[] = {256, 128};
-  const gemm::Choice c = gemm::pick(M, N, cand, 2, 0);
+  const gemm::Choice c = gemm::pick(M, N, cand, 2, force ? force : 2);
   if (d == 128) {
     if (c.bn == 128)
       return c.pair ? gemm::launch2<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)

@@ -349,6 +349,18 @@ __global__ void __launch_bounds__(THREADS) label_head_kernel(const __nv_bfloat16
   for (int l = threadIdx.x; l < nl; l += THREADS) probs[l0 + l] = expf(logits[l] - mx) / se;
 }
 
+// RoPE table by position: table[p][i] = (cos, sin)(p * inv_freq[i]) in FP32, the values the reference computes per
+// step (`f = positions * inv_freq`, `f.cos()`, `f.sin()`).
+__global__ void __launch_bounds__(256) rope_table_kernel(const float* __restrict__ inv_freq, int half, int rows,
+                                                        float2* __restrict__ table) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * half) return;
+  const int p = (int)(i / half), f = (int)(i % half);
+  float sn, cs;
+  sincosf((float)p * inv_freq[f], &sn, &cs);
+  table[i] = make_float2(cs, sn);
+}
+
 }  // namespace rows
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -447,6 +459,19 @@ extern "C" int morj_mlp_epilogue(const void* d, void* x, void* h_out, const void
                          (const __nv_bfloat16*)w_post, (const __nv_bfloat16*)scalar, (const __nv_bfloat16*)w_next, H,
                          eps, has_next)));
   return check_launch("mlp_epilogue_kernel");
+}
+
+extern "C" int morj_rope_table(const float* inv_freq, int half, int rows, void* table, void* stream) {
+  if (rows == 0) return MORJ_OK;
+  if (!inv_freq || !table || half <= 0 || half % 2 || rows < 0)
+    return set_error(MORJ_ERR_ARG, "morj_rope_table: bad arguments (half=%d rows=%d)", half, rows);
+  if (reinterpret_cast<uintptr_t>(table) & 15)
+    return set_error(MORJ_ERR_ARG, "morj_rope_table: table must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long n = (long long)rows * half;
+  rows::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(inv_freq, half, rows,
+                                                                       reinterpret_cast<float2*>(table));
+  return check_launch("rope_table_kernel");
 }
 
 extern "C" int morj_qkv_post(const void* qkv, long long ld, int n, int hq, int hk, int has_v, int d,

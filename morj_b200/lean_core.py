@@ -228,6 +228,9 @@ class LeanGemma4:
         rot = 1.0 / (rp['full_attention']['rope_theta'] ** (
             torch.arange(0, 2 * angles, 2, dtype=torch.int64).float() / gd))
         self.inv_freq['full_attention'] = torch.cat([rot, torch.zeros(gd // 2 - angles)]).float().to(self.device)
+        # (cos, sin) of position x inv_freq, by position, per kind: the reference's per-step tables
+        # (`lean_core.py:636-640`), built once and grown with the longest position seen (`_rope`)
+        self.rope = {}
         self.prune_last = True
         self.kv_bytes = sum(2 * 2 * self.geom[k][0] * self.geom[k][1] for k in self.types)
         self.retain_budget = retain_budget_gb * 2**30
@@ -563,6 +566,17 @@ class LeanGemma4:
             else:
                 dist.all_reduce(t, group=self.tp_group)
 
+    def _rope(self, kind, max_pos):
+        """The RoPE table of `kind` covering positions 0..max_pos (grown to the next power of two, at least 4096)."""
+        tab = self.rope.get(kind)
+        if tab is None or tab.shape[0] <= max_pos:
+            rows = max(4096, 1 << int(max_pos).bit_length())
+            inv = self.inv_freq[kind]
+            tab = torch.empty(rows, inv.numel(), 2, dtype=torch.float32, device=self.device)
+            self._k('rows', 'morj_rope_table', inv.data_ptr(), inv.numel(), rows, tab.data_ptr(), self._stream())
+            self.rope[kind] = tab
+        return tab
+
     def _qkv(self, a, layer, row0, M, hq, hk, has_v, d, kind, positions, slots, q_out, k_pool, v_pool):
         """QKV projection with the fused head norm + RoPE + pool scatter (`morj_gemm_qkv_rope`); `row0` skips the q
         rows of the fused weight for the K/V-only call."""
@@ -571,8 +585,9 @@ class LeanGemma4:
         n_out = (hq + (2 if has_v else 1) * hk) * d
         flops = 2 * M * n_out * H
         wp = w.data_ptr() + row0 * w.stride(0) * w.element_size()
+        rope = self.rope[kind]
         self._k('gemm_qkv', 'morj_gemm_qkv_rope', a.data_ptr(), a.stride(0), wp, w.stride(0), M, H, hq, hk, has_v,
-                d, layer['q_norm'].data_ptr(), layer['k_norm'].data_ptr(), positions, self.inv_freq[kind].data_ptr(),
+                d, layer['q_norm'].data_ptr(), layer['k_norm'].data_ptr(), positions, rope.data_ptr(), rope.shape[0],
                 slots, self.eps, _ptr(q_out), _ptr(k_pool), _ptr(v_pool), self._stream(), flops=flops)
 
     def _attention(self, q, k_pool, v_pool, out, t, qo, kv_indptr, kv_indices, n_seg, n_bidir, kind, work, n_work):
@@ -594,6 +609,9 @@ class LeanGemma4:
         n_seg = len(st['qo_indptr']) - 1
         x = torch.empty(n, H, dtype=bf, device=dev)
         h = torch.empty(n, H, dtype=bf, device=dev)
+        max_pos = int(np.max(st['positions'])) if n else 0
+        for kind in set(self.types):
+            self._rope(kind, max_pos)
         feat = req.features
         self._k('rows', 'morj_embed_rmsnorm', t.ptr('tokens'), t.ptr('feature_row') if feat is not None else None,
                  _ptr(feat), self.embed.data_ptr(), n, H, self.embed_scale, self.layers[0]['in_ln'].data_ptr(), eps,

@@ -307,11 +307,13 @@ def test_row_gather_scatter_and_reference_geglu():
     close(out, geglu(gu))
 
 
+@pytest.mark.parametrize('force', [0, 0x100, 0x200])
 @pytest.mark.parametrize('M,H,d,hq,hk,has_v', [(77, 256, 64, 4, 2, 1), (300, 256, 64, 4, 2, 0),
                                                (2040, 5376, 128, 32, 16, 1), (517, 5376, 128, 32, 16, 0),
                                                (9, 5376, 128, 32, 0, 1), (130, 512, 128, 0, 16, 0)])
-def test_fused_qkv_gemm_matches_gemm_then_oracle_head_epilogue(M, H, d, hq, hk, has_v):
-    """morj_gemm_qkv_rope == BF16 projection followed by the reference head epilogue (`_qkv_post`)."""
+def test_fused_qkv_gemm_matches_gemm_then_oracle_head_epilogue(M, H, d, hq, hk, has_v, force):
+    """morj_gemm_qkv_rope == BF16 projection followed by the reference head epilogue (`_qkv_post`), with the kernel
+    chosen per shape, the SM-pair kernel and the one-CTA kernel."""
     from oracle.lean_oracle import qkv_post, rope_tables
     g = torch.Generator(device=DEV).manual_seed(M + hq)
     rows = (hq + (2 if has_v else 1) * hk) * d
@@ -327,8 +329,10 @@ def test_fused_qkv_gemm_matches_gemm_then_oracle_head_epilogue(M, H, d, hq, hk, 
     kp = torch.zeros(cap, max(hk, 1), d, device=DEV, dtype=torch.bfloat16)
     vp = torch.zeros(cap, max(hk, 1), d, device=DEV, dtype=torch.bfloat16)
     pos_d, sl_d = i32(pos), i32(slots)
-    nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, has_v, d, qn.data_ptr(),
-             kn.data_ptr(), pos_d.data_ptr(), inv.data_ptr(), sl_d.data_ptr() if hk else None, 1e-6,
+    rope = torch.empty(9000, d // 2, 2, device=DEV)
+    nat.call('morj_rope_table', inv.data_ptr(), d // 2, 9000, rope.data_ptr(), stream())
+    nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, has_v | force, d, qn.data_ptr(),
+             kn.data_ptr(), pos_d.data_ptr(), rope.data_ptr(), 9000, sl_d.data_ptr() if hk else None, 1e-6,
              q_out.data_ptr() if hq else None, kp.data_ptr() if hk else None, vp.data_ptr() if hk else None, stream())
     torch.cuda.synchronize()
     proj = (a.float() @ w.float().T).bfloat16().cpu()
@@ -341,6 +345,44 @@ def test_fused_qkv_gemm_matches_gemm_then_oracle_head_epilogue(M, H, d, hq, hk, 
     if hk:
         close(kp[torch.as_tensor(slots)], k)
         close(vp[torch.as_tensor(slots)], v)
+
+
+def test_rope_table_matches_torch_cos_sin():
+    """morj_rope_table == the reference's FP32 `f.cos()`, `f.sin()` of position x inv_freq (`lean_core.py:636-640`),
+    on the device, including the proportional partial table (zero frequencies)."""
+    inv = torch.cat([1.0 / (10000 ** (torch.arange(0, 96, 2).float() / 128)), torch.zeros(16)]).to(DEV)
+    rows = 70000
+    tab = torch.empty(rows, 64, 2, device=DEV)
+    nat.call('morj_rope_table', inv.data_ptr(), 64, rows, tab.data_ptr(), stream())
+    f = torch.arange(rows, device=DEV, dtype=torch.float32)[:, None] * inv[None]
+    torch.testing.assert_close(tab[..., 0], f.cos(), rtol=0, atol=2e-7)
+    torch.testing.assert_close(tab[..., 1], f.sin(), rtol=0, atol=2e-7)
+    with pytest.raises(ValueError):
+        nat.call('morj_rope_table', inv.data_ptr(), 63, 10, tab.data_ptr(), stream())
+
+
+def test_fused_qkv_position_outside_table_sets_device_error():
+    """A position beyond the RoPE table is reported through the device error word and its row is left unwritten."""
+    M, H, d, hq, hk = 130, 256, 64, 4, 2
+    a = torch.randn(M, H, device=DEV).to(torch.bfloat16)
+    w = (torch.randn((hq + 2 * hk) * d, H, device=DEV) * 0.05).to(torch.bfloat16)
+    qn = torch.ones(d, device=DEV, dtype=torch.bfloat16)
+    inv = (1.0 / (10000 ** (torch.arange(0, d, 2).float() / d))).to(DEV)
+    rope = torch.empty(100, d // 2, 2, device=DEV)
+    nat.call('morj_rope_table', inv.data_ptr(), d // 2, 100, rope.data_ptr(), stream())
+    pos = i32(np.arange(M) % 100)
+    pos[77] = 100  # one past the table
+    slots = i32(np.arange(M))
+    q_out = torch.zeros(M, hq, d, device=DEV, dtype=torch.bfloat16)
+    kp = torch.zeros(M, hk, d, device=DEV, dtype=torch.bfloat16)
+    vp = torch.zeros(M, hk, d, device=DEV, dtype=torch.bfloat16)
+    nat.device_error(stream())
+    nat.call('morj_gemm_qkv_rope', a.data_ptr(), H, w.data_ptr(), H, M, H, hq, hk, 1, d, qn.data_ptr(),
+             qn.data_ptr(), pos.data_ptr(), rope.data_ptr(), 100, slots.data_ptr(), 1e-6, q_out.data_ptr(),
+             kp.data_ptr(), vp.data_ptr(), stream())
+    assert nat.device_error(stream()) == 0x301
+    assert (q_out[77] == 0).all() and (kp[77] == 0).all() and (vp[77] == 0).all()
+    assert (q_out[76] != 0).any()
 
 
 @pytest.mark.parametrize('force', [0x100, 0x200])

@@ -286,6 +286,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency', 'sweep'])
+    ap.add_argument('--tp-comm', default='peer', choices=['peer', 'nccl'],
+                    help='tensor parallelism: reduce over peer memory fused with the epilogues, or NCCL all-reduce')
     ap.add_argument('--mode', default='replicas', choices=['replicas', 'tp'],
                     help='replicas: one model per GPU on independent trees (weak scaling); tp: one tree, the model '
                          'sharded over all GPUs with NCCL all-reduces (strong scaling, single-tree latency)')
@@ -331,7 +333,8 @@ def main():
     tp = args.mode == 'tp' and world > 1
     top = w.gemma31b_config()
     t_init = time.perf_counter()
-    model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD if tp else None)
+    model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD if tp else None,
+                                   tp_comm=args.tp_comm)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t_init
     tree_in, desc = workload(args.workload, 0 if tp else rank)
@@ -459,7 +462,9 @@ def main():
             dtype='bf16',
             data='synthetic (seeded random-init weights N(0, 0.02), uniform token ids)',
             config=dict(workload=f'31B-class Gemma-style decoder, {desc}', tokens=tokens,
-                        parallelism=(f'tensor parallel x{world} (NCCL all-reduce after O and down)' if tp else
+                        parallelism=((f'tensor parallel x{world} (O/down partials stored to the row owners over '
+                                      f'NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else
+                                      f'tensor parallel x{world} (NCCL all-reduce after O and down)') if tp else
                                      f'replicas x{world} (independent trees, no collective)'),
                         l2='inputs larger than L2 (52 GB of weights streamed per step)',
                         tflops_per_tree_specified=round((flops_lin + flops_attn) / 1e12, 2)),
@@ -481,6 +486,10 @@ def main():
             line['cpu_baseline'] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
+        if model.peer is not None:  # every rank is done with the peers' buffers before any frees its own
+            barrier()
+            model.peer.close()
+            barrier()
         dist.destroy_process_group()
 
 

@@ -149,6 +149,57 @@ int morj_label_head(const void* x, long long ld_x, const int* seq_row, const int
 /* Reference-layout GeGLU (unfused path): out[i, j] = bf16(gelu_tanh(gu[i, j]) * gu[i, F + j]), gu: [n, 2F]. */
 int morj_geglu(const void* gu, int n, int F, void* out, void* stream);
 
+/* ---- tensor parallelism over peer memory (no counterpart in the reference, which runs one GPU per model; this
+ * replaces the NCCL all-reduce after the row-parallel O and down projections of a T-way sharded model) ----------
+ *
+ * Rows are owned in blocks of 128: row block b belongs to rank b % world. Each rank's row-parallel GEMM stores its
+ * BF16 partial tile straight into the owner's receive area (NVLink stores to peer memory) and counts the columns it
+ * delivered on the owner's per-block counter; the owner's reduce kernel waits for all ranks' columns, sums the
+ * partials in rank order in FP32, rounds to BF16 (the value an NCCL BF16 all-reduce gives for two ranks), applies
+ * the post-attention or post-MLP epilogue to its own rows, and stores the new h rows (and, when asked, x rows) into
+ * every rank's buffers, counting rows on their per-block counters. A wait kernel then holds the stream until every
+ * row block of h has arrived. Counters only grow: the caller passes cumulative targets (site = one O or down
+ * reduction; after s sites every block's partial counter reaches s * world * 4 * H and its row counter s * 128),
+ * and blocks past a call's rows are padded by the reduce kernel so the targets hold for every block.
+ * Every wait is bounded (2 s): on expiry the kernel records MORJ device code 0x104 / 0x105 and returns. */
+#define MORJ_MAX_RANKS 8
+typedef struct morj_peer {
+  int world;       /* ranks (1..8) */
+  int rank;        /* this rank */
+  int max_blocks;  /* row blocks of 128 each buffer holds */
+  int hidden;      /* H, columns of every exchanged row */
+  int slab_rows;   /* rows of one source rank's slab in a receive area: ceil(max_blocks / world) * 128 */
+  int pad_;
+  void* recv[MORJ_MAX_RANKS];                  /* rank r's receive area: world slabs of slab_rows x H BF16 */
+  void* x[MORJ_MAX_RANKS];                     /* rank r's residual rows, [max_blocks * 128, H] BF16 */
+  void* h[MORJ_MAX_RANKS];                     /* rank r's normed rows, [max_blocks * 128, H] BF16 */
+  unsigned long long* partials[MORJ_MAX_RANKS]; /* rank r's partial-column counters, [max_blocks] */
+  unsigned long long* rows[MORJ_MAX_RANKS];     /* rank r's row counters, [max_blocks] */
+} morj_peer_t;
+
+/* CUDA IPC export of the device allocation holding `ptr` (handle: MORJ_IPC_HANDLE_BYTES bytes: the CUDA handle of
+ * the allocation and ptr's offset in it), import on another process (peer access enabled; *ptr = the same byte),
+ * and close of an imported pointer (with its handle). */
+#define MORJ_IPC_HANDLE_BYTES 72
+int morj_ipc_export(const void* ptr, void* handle);
+int morj_ipc_import(const void* handle, void** ptr);
+int morj_ipc_close(void* ptr, const void* handle);
+
+/* Row-parallel GEMM whose epilogue delivers its BF16 partial tiles to the owners (C = A . B^T, [M, N], N = hidden,
+ * M <= max_blocks * 128); the kernel is chosen per shape as for morj_gemm_bf16. */
+int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                        const morj_peer_t* peer, void* stream);
+
+/* The owner's reduction of one site for rows [0, n): mode 0 = post-attention epilogue (w_a = post_attn,
+ * w_b = pre_ff; morj_attn_epilogue's math), mode 1 = post-MLP epilogue (w_a = post_ff, scalar, w_b = next input
+ * norm, has_next; morj_mlp_epilogue's math). x rows go to the peers only when push_x != 0. partial_target: the
+ * cumulative partial count to wait for. */
+int morj_peer_reduce(const morj_peer_t* peer, int mode, int n, const void* w_a, const void* scalar, const void* w_b,
+                     float eps, int has_next, int push_x, unsigned long long partial_target, void* stream);
+
+/* Hold the stream until every row block below n has reached row_target on this rank's row counters. */
+int morj_peer_wait(const morj_peer_t* peer, int n, unsigned long long row_target, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,7 +40,23 @@ SIGNATURES = {
     'morj_scatter_rows': [P, LL, P, I, I, P, LL, P],
     'morj_label_head': [P, LL, P, P, P, I, P, P, I, F, F, P, P],
     'morj_geglu': [P, I, I, P, P],
+    'morj_ipc_export': [P, P],
+    'morj_ipc_import': [P, ctypes.POINTER(P)],
+    'morj_ipc_close': [P, P],
+    'morj_gemm_bf16_peer': [P, LL, P, LL, I, I, I, P, P],
+    'morj_peer_reduce': [P, I, I, P, P, P, F, I, I, ctypes.c_ulonglong, P],
+    'morj_peer_wait': [P, I, ctypes.c_ulonglong, P],
 }
+
+IPC_HANDLE_BYTES = 72
+MAX_RANKS = 8
+
+
+class PeerDesc(ctypes.Structure):
+    """`morj_peer_t`: the exchange buffers of every rank of a tensor-parallel group, as this process sees them."""
+    _fields_ = [('world', I), ('rank', I), ('max_blocks', I), ('hidden', I), ('slab_rows', I), ('pad_', I),
+                ('recv', P * MAX_RANKS), ('x', P * MAX_RANKS), ('h', P * MAX_RANKS),
+                ('partials', P * MAX_RANKS), ('rows', P * MAX_RANKS)]
 
 
 class NativeFailure(RuntimeError):

@@ -26,6 +26,8 @@ enum DeviceError : int {
   kErrTimeoutGemmProducer = 0x101,
   kErrTimeoutGemmMma = 0x102,
   kErrTimeoutGemmEpilogue = 0x103,
+  kErrTimeoutPeerPartials = 0x104,
+  kErrTimeoutPeerRows = 0x105,
   kErrTimeoutAttention = 0x201,
   kErrBadIndex = 0x301,
   kErrBadAlignment = 0x302,
@@ -297,6 +299,53 @@ MORJ_DEV void unpack8_bf16(uint4 u, float (&v)[8]) {
   const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
   v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y, v[4] = c.x, v[5] = c.y, v[6] = d.x, v[7] = d.y;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// row helpers (one CTA per token row, 8-wide BF16 vectors, FP32 reductions)
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int ROW_THREADS = 256;
+
+MORJ_DEV float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();  // red may still be read by a previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x / 32;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+MORJ_DEV void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+MORJ_DEV void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// hidden sizes up to 16384: VPT = 8-element vectors per thread of a ROW_THREADS-thread row CTA
+inline int vpt_for(int H) { return (H / 8 + ROW_THREADS - 1) / ROW_THREADS; }
+#define MORJ_VPT_SWITCH(H, CALL)                                                      \
+  switch (vpt_for(H)) {                                                               \
+    case 1: { constexpr int V = 1; CALL; break; }                                     \
+    case 2: { constexpr int V = 2; CALL; break; }                                     \
+    case 3: { constexpr int V = 3; CALL; break; }                                     \
+    case 4: { constexpr int V = 4; CALL; break; }                                     \
+    case 5: { constexpr int V = 5; CALL; break; }                                     \
+    case 6: { constexpr int V = 6; CALL; break; }                                     \
+    case 7: { constexpr int V = 7; CALL; break; }                                     \
+    case 8: { constexpr int V = 8; CALL; break; }                                     \
+    default: return set_error(MORJ_ERR_UNSUPPORTED, "hidden size %d above 16384", H); \
+  }
 
 // tanh-approximated GELU from its definition 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
 MORJ_DEV float gelu_tanh(float x) {

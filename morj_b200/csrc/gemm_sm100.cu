@@ -24,13 +24,15 @@ constexpr int GROUP_M = 16;
 
 // Tile width BN (a multiple of 16, at most 256): the host picks it per shape so the tile count fills whole waves of
 // the SMs; the stage ring is as deep as shared memory allows.
-template <int BN>
+// EXTRA: shared memory for the epilogue's row staging (the partial-delivery epilogue), after the barriers.
+template <int BN, int EXTRA = 0>
 struct Cfg {
   static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "tile width");
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (220 * 1024) / STAGE_BYTES > 6 ? 6 : (220 * 1024) / STAGE_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGES =
+      (220 * 1024 - EXTRA) / STAGE_BYTES > 6 ? 6 : (220 * 1024 - EXTRA) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EXTRA;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
 };
 
@@ -53,6 +55,20 @@ struct QkvEpi {
   __nv_bfloat16* k_pool;
   __nv_bfloat16* v_pool;
 };
+
+// Operands of the partial-delivery epilogue (tensor parallelism over peer memory): row block b of the output goes
+// to rank b % world's receive area, slab `rank`, and the delivered columns are counted on that rank's counter b.
+constexpr int EPI_PEER = 4;
+constexpr int PEER_STAGING = 4 * 4096;  // per epilogue warp: 32 rows x 64 BF16 columns
+struct PeerEpi {
+  __nv_bfloat16* recv[MORJ_MAX_RANKS];
+  unsigned long long* partials[MORJ_MAX_RANKS];
+  int world, rank, slab_rows;
+};
+
+MORJ_DEV void red_release_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 MORJ_DEV void store32_bf16(__nv_bfloat16* dst, const float (&v)[32]) {
 #pragma unroll
@@ -179,32 +195,95 @@ MORJ_DEV TileCoord tile_coord(int t, int num_m, int num_n) {
   return {first_m + local % gm, local / gm};
 }
 
-template <int EPI, int BN>
-MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv_bfloat16* C, long long ldc, int N) {
-  if constexpr (EPI == MORJ_EPI_STORE) {
-    __nv_bfloat16* crow = C + (size_t)row * ldc;
-    const int lim = min(N, (n_blk + 1) * BN);  // this tile's columns (the last 32-column load may run past BN)
+// BF16 store of one accumulator row (this thread's) of tile column block n_blk into crow[n_blk * BN ...].
+template <int BN>
+MORJ_DEV void store_row(uint32_t tacc, __nv_bfloat16* crow, int n_blk, bool row_ok, int N) {
+  const int lim = min(N, (n_blk + 1) * BN);  // this tile's columns (the last 32-column load may run past BN)
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tacc + c, r);
-      tmem_wait_ld();
-      const int col = n_blk * BN + c;
-      if (row_ok && col < lim) {
-        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(tacc + c, r);
+    tmem_wait_ld();
+    const int col = n_blk * BN + c;
+    if (row_ok && col < lim) {
+      uint4* dst = reinterpret_cast<uint4*>(crow + col);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          if (col + v * 8 < lim) {
-            uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-            pk.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-            pk.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-            pk.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-            dst[v] = pk;
-          }
+      for (int v = 0; v < 4; ++v) {
+        if (col + v * 8 < lim) {
+          uint4 pk;
+          pk.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+          pk.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+          pk.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+          pk.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+          dst[v] = pk;
         }
       }
     }
+  }
+}
+
+// Partial-delivery epilogue: this warp's 32 rows of the tile go to the row block's owner (over NVLink unless the
+// owner is this rank). Each 64-column slice is staged in shared memory (4 KB per warp, 16-byte units XOR-swizzled by
+// row) and written out as whole 128-byte row segments, four rows per warp store. Once the tile's rows are out the
+// warp counts the tile's columns on the owner's counter (`peer_arrive`: system fence, then a release add); the
+// counter and the count are returned for that. Row blocks wholly past M (the pair kernel's padding) neither store
+// nor count.
+template <int BN>
+MORJ_DEV void epilogue_peer(uint32_t tacc, int row, int n_blk, int M, int N, const PeerEpi& pe, int lane,
+                            uint4* stage, unsigned long long** count, unsigned long long* cols) {
+  const int blk = row / 128;
+  if (blk * 128 >= M) return;
+  const int owner = blk % pe.world;
+  const int row0 = row - lane;  // the warp's first row
+  const size_t local0 = (size_t)(blk / pe.world) * 128 + (row0 & 127);
+  __nv_bfloat16* base = pe.recv[owner] + ((size_t)pe.rank * pe.slab_rows + local0) * N;
+  const int lim = min(N, (n_blk + 1) * BN);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t r[32];
+      tmem_ld32(tacc + c + 32 * half, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint4 pk;
+        pk.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+        pk.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+        pk.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+        pk.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+        stage[lane * 8 + ((half * 4 + v) ^ (lane & 7))] = pk;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = it * 32 + lane;
+      const int rr = idx >> 3, chunk = idx & 7;
+      const int col = n_blk * BN + c + chunk * 8;
+      if (row0 + rr < M && col < lim)
+        *reinterpret_cast<uint4*>(base + (size_t)rr * N + col) = stage[rr * 8 + (chunk ^ (rr & 7))];
+    }
+    __syncwarp();
+  }
+  *count = pe.partials[owner] + blk;
+  *cols = (unsigned long long)(lim - n_blk * BN);
+}
+
+// The arrival of a delivered tile (deferred to the warp's next accumulator wait, where the system fence's round trip
+// is hidden under the main loop): every lane's stores are visible system-wide before lane 0's release add.
+MORJ_DEV void peer_arrive(unsigned long long*& count, unsigned long long cols, int lane) {
+  if (count == nullptr) return;
+  __threadfence_system();
+  __syncwarp();
+  if (lane == 0) red_release_sys_add(count, cols);
+  count = nullptr;
+}
+
+template <int EPI, int BN>
+MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv_bfloat16* C, long long ldc, int N) {
+  if constexpr (EPI == MORJ_EPI_STORE) {
+    store_row<BN>(tacc, C + (size_t)row * ldc, n_blk, row_ok, N);
   } else {
     // gate columns [0, 128), up columns [128, 256) of this tile -> 128 outputs
     const int F = N / 2;
@@ -242,8 +321,9 @@ MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv
 template <int EPI, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe) {
-  using C_ = Cfg<BN>;
+                __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe,
+                const PeerEpi pe) {
+  using C_ = Cfg<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -365,11 +445,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
+    unsigned long long* pend = nullptr;  // partial-delivery epilogue: the arrival still to post
+    unsigned long long pend_cols = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       const TileCoord tc = tile_coord(t, num_m, num_n);
       // lane 0 waits for the accumulator; the warp follows its verdict (tcgen05.ld below is warp-collective)
       int ok = lane == 0 ? (int)mbar_wait(accf0 + 8 * acc, acc_phase, abort, kErrTimeoutGemmEpilogue) : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
+      if constexpr (EPI == EPI_PEER) peer_arrive(pend, pend_cols, lane);
       if (!ok) break;
       tc_fence_after();
       const int row = tc.m * BM + quarter * 32 + lane;
@@ -378,6 +461,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         epilogue_qkv<BN, 128>(tacc, row, tc.n, row < M, qe, N);
       } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
         epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
+      } else if constexpr (EPI == EPI_PEER) {
+        epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, lane,
+                          reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256 + quarter * 4096), &pend,
+                          &pend_cols);
       } else {
         epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
       }
@@ -388,6 +475,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         acc_phase ^= 1;
       }
     }
+    if constexpr (EPI == EPI_PEER) peer_arrive(pend, pend_cols, lane);
   }
 
   tc_fence_before();
@@ -405,21 +493,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 // half of the B tile per k-block, so the L2-to-shared-memory traffic per FLOP drops by a third against the one-CTA
 // kernel. The epilogues are the one-CTA kernel's (each CTA drains its own 128 rows).
 // ---------------------------------------------------------------------------------------------------------------
-template <int BN>
+template <int BN, int EXTRA = 0>
 struct Cfg2 {
   static_assert(BN % 32 == 0 || BN % 16 == 0, "tile width");
   static constexpr int B_HALF_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_HALF_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGES =
+      (200 * 1024 - EXTRA) / STAGE_BYTES > 8 ? 8 : (200 * 1024 - EXTRA) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EXTRA;
   static constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN);
 };
 
 template <int EPI, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe) {
-  using C_ = Cfg2<BN>;
+                 __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe,
+                 const PeerEpi pe) {
+  using C_ = Cfg2<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -548,10 +638,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t acce_leader = map_shared(acce0, 0);
     int acc = 0;
     uint32_t acc_phase = 0;
+    unsigned long long* pend = nullptr;  // partial-delivery epilogue: the arrival still to post
+    unsigned long long pend_cols = 0;
     for (int t = cluster; t < tiles; t += n_clusters) {
       const TileCoord tc = tile_coord(t, num_m, num_n);
       int ok = lane == 0 ? (int)mbar_wait(accf0 + 8 * acc, acc_phase, abort, kErrTimeoutGemmEpilogue) : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
+      if constexpr (EPI == EPI_PEER) peer_arrive(pend, pend_cols, lane);
       if (!ok) break;
       tc_fence_after();
       const int row = tc.m * 2 * BM + rank * BM + quarter * 32 + lane;
@@ -560,6 +653,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         epilogue_qkv<BN, 128>(tacc, row, tc.n, row < M, qe, N);
       } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
         epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
+      } else if constexpr (EPI == EPI_PEER) {
+        epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, lane,
+                          reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256 + quarter * 4096), &pend,
+                          &pend_cols);
       } else {
         epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
       }
@@ -571,6 +668,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         acc_phase ^= 1;
       }
     }
+    if constexpr (EPI == EPI_PEER) peer_arrive(pend, pend_cols, lane);
   }
 
   tc_fence_before();
@@ -644,8 +742,8 @@ static int make_map(CUtensorMap* map, const void* ptr, long long rows, long long
 
 template <int EPI, int BN>
 static int launch(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
-                  int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}) {
-  using C_ = Cfg<BN>;
+                  int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}, const PeerEpi& pe = PeerEpi{}) {
+  using C_ = Cfg<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -661,14 +759,14 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   gemm_kernel<EPI, BN><<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                                                   M, N, K, qe);
+                                                                   M, N, K, qe, pe);
   return check_launch("gemm_kernel");
 }
 
 template <int EPI, int BN>
 static int launch2(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
-                   int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}) {
-  using C_ = Cfg2<BN>;
+                   int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}, const PeerEpi& pe = PeerEpi{}) {
+  using C_ = Cfg2<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -685,7 +783,7 @@ static int launch2(const void* A, long long lda, const void* B, long long ldb, v
   const int pairs = num_sms() / 2;
   const int clusters = tiles < pairs ? tiles : pairs;
   gemm2_kernel<EPI, BN><<<2 * clusters, THREADS, C_::SMEM_BYTES, stream>>>(
-      ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe);
+      ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe);
   return check_launch("gemm2_kernel");
 }
 
@@ -768,6 +866,49 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
     return gemm::launch<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
   }
   return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: unknown epilogue %d", epilogue);
+}
+
+extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                                   const morj_peer_t* peer, void* stream) {
+  using namespace morj;
+  if (M == 0) return MORJ_OK;
+  if (!A || !B || !peer || M < 0 || N <= 0 || K <= 0)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: bad pointers or sizes (M=%d N=%d K=%d)", M, N, K);
+  if (peer->world < 1 || peer->world > MORJ_MAX_RANKS || peer->rank < 0 || peer->rank >= peer->world ||
+      N != peer->hidden || M > peer->max_blocks * 128 ||
+      peer->slab_rows < ((peer->max_blocks + peer->world - 1) / peer->world) * 128)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: exchange buffers do not fit (M=%d N=%d)", M, N);
+  if (N % 16 || K % 8 || lda % 8 || ldb % 8 || lda < K || ldb < K)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: N % 16, K and leading dimensions % 8 required");
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15)
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: pointers must be 16-byte aligned");
+  gemm::PeerEpi pe{};
+  for (int r = 0; r < peer->world; ++r) {
+    if (!peer->recv[r] || !peer->partials[r] || (reinterpret_cast<uintptr_t>(peer->recv[r]) & 15))
+      return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's buffers are missing or unaligned", r);
+    pe.recv[r] = reinterpret_cast<__nv_bfloat16*>(peer->recv[r]);
+    pe.partials[r] = peer->partials[r];
+  }
+  pe.world = peer->world;
+  pe.rank = peer->rank;
+  pe.slab_rows = peer->slab_rows;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  static const int cand[] = {256, 208, 192, 128};
+  const gemm::Choice c = gemm::pick(M, N, cand, 4, 0);
+  const gemm::QkvEpi qe{};
+#define MORJ_PEER_CASE(W)                                                                                        \
+  case W:                                                                                                        \
+    return c.pair ? gemm::launch2<gemm::EPI_PEER, W>(A, lda, B, ldb, nullptr, 0, M, N, K, s, qe, pe)             \
+                  : gemm::launch<gemm::EPI_PEER, W>(A, lda, B, ldb, nullptr, 0, M, N, K, s, qe, pe);
+  switch (c.bn) {
+    MORJ_PEER_CASE(208)
+    MORJ_PEER_CASE(192)
+    MORJ_PEER_CASE(128)
+    default:
+      return c.pair ? gemm::launch2<gemm::EPI_PEER, 256>(A, lda, B, ldb, nullptr, 0, M, N, K, s, qe, pe)
+                    : gemm::launch<gemm::EPI_PEER, 256>(A, lda, B, ldb, nullptr, 0, M, N, K, s, qe, pe);
+  }
+#undef MORJ_PEER_CASE
 }
 
 extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, long long ldw, int M, int K, int hq,

@@ -16,19 +16,6 @@ namespace rows {
 
 constexpr int THREADS = 256;
 
-MORJ_DEV float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  __syncthreads();  // red may still be read by a previous reduction
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-  const int nw = blockDim.x / 32;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
-
 MORJ_DEV float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -40,20 +27,6 @@ MORJ_DEV float block_max(float v, float* red) {
   const int nw = blockDim.x / 32;
   for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
   return t;
-}
-
-MORJ_DEV void load8(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
-  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
-}
-MORJ_DEV void store8(__nv_bfloat16* p, const float (&v)[8]) {
-  uint4 u;
-  u.x = pack_bf16x2(v[0], v[1]);
-  u.y = pack_bf16x2(v[2], v[3]);
-  u.z = pack_bf16x2(v[4], v[5]);
-  u.w = pack_bf16x2(v[6], v[7]);
-  *reinterpret_cast<uint4*>(p) = u;
 }
 
 // ---- embedding + image rows + input RMSNorm -------------------------------------------------------------------
@@ -388,20 +361,6 @@ int check_launch(const char* what) {
 
 using namespace morj;
 
-static int vpt_for(int H) { return (H / 8 + rows::THREADS - 1) / rows::THREADS; }
-
-#define MORJ_VPT_SWITCH(H, CALL)                                                      \
-  switch (vpt_for(H)) {                                                               \
-    case 1: { constexpr int V = 1; CALL; break; }                                     \
-    case 2: { constexpr int V = 2; CALL; break; }                                     \
-    case 3: { constexpr int V = 3; CALL; break; }                                     \
-    case 4: { constexpr int V = 4; CALL; break; }                                     \
-    case 5: { constexpr int V = 5; CALL; break; }                                     \
-    case 6: { constexpr int V = 6; CALL; break; }                                     \
-    case 7: { constexpr int V = 7; CALL; break; }                                     \
-    case 8: { constexpr int V = 8; CALL; break; }                                     \
-    default: return set_error(MORJ_ERR_UNSUPPORTED, "hidden size %d above 16384", H); \
-  }
 
 extern "C" int morj_version(void) { return 100; }
 

@@ -135,25 +135,28 @@ class _Tables:
 
 class LeanGemma4:
     def __init__(self, model_dir, device='cuda', workspace_mb=512, retain_budget_gb=10.0, single_max=16384,
-                 step_tokens=8192, *, tp_group=None):
+                 step_tokens=8192, *, tp_group=None, tp_comm='peer'):
         """Load a safetensors checkpoint (`config.json["text_config"]` + `model.language_model.*` tensors) as the
         reference does (`lean_core.py:340-416`). `workspace_mb` is accepted for interface compatibility; the tree
         attention kernel needs no workspace. `tp_group`: a torch.distributed process group (NCCL) to shard the model
-        over for tensor parallelism (`morj_b200.tp`); None runs the whole model on this GPU."""
+        over for tensor parallelism (`morj_b200.tp`); None runs the whole model on this GPU. `tp_comm`: 'peer'
+        reduces the row-parallel projections over peer memory fused with their epilogues (`tp.PeerExchange`),
+        'nccl' with an NCCL all-reduce followed by the replicated epilogues."""
         top, get = open_checkpoint(model_dir, device)
-        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens, tp_group)
+        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens, tp_group, tp_comm)
 
     @classmethod
     def from_state(cls, top, state, device='cuda', retain_budget_gb=10.0, single_max=16384, step_tokens=8192,
-                   tp_group=None):
+                   tp_group=None, tp_comm='peer'):
         """An engine over an in-memory state dict in the checkpoint's key layout (tensors on any device)."""
         self = cls.__new__(cls)
-        self._setup(top, lambda k: state[k].to(device), device, retain_budget_gb, single_max, step_tokens, tp_group)
+        self._setup(top, lambda k: state[k].to(device), device, retain_budget_gb, single_max, step_tokens, tp_group,
+                    tp_comm)
         return self
 
     @classmethod
     def random_init(cls, top, seed=0, device='cuda', std=0.02, norm_std=0.1, retain_budget_gb=10.0,
-                    single_max=16384, step_tokens=8192, tp_group=None):
+                    single_max=16384, step_tokens=8192, tp_group=None, tp_comm='peer'):
         """An engine over seeded random-init weights generated on `device` (no checkpoint on disk); tensors are drawn
         in checkpoint order and handed over one at a time, so the peak memory is the model plus one layer."""
         gen = iter_random_state(top, seed=seed, std=std, norm_std=norm_std, device=device)
@@ -165,11 +168,14 @@ class LeanGemma4:
                 cache[k] = t
             return cache.pop(key)
         self = cls.__new__(cls)
-        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens, tp_group)
+        self._setup(top, get, device, retain_budget_gb, single_max, step_tokens, tp_group, tp_comm)
         return self
 
-    def _setup(self, top, get, device, retain_budget_gb, single_max, step_tokens, tp_group=None):
+    def _setup(self, top, get, device, retain_budget_gb, single_max, step_tokens, tp_group=None, tp_comm='peer'):
+        if tp_comm not in ('peer', 'nccl'):
+            raise ValueError(f"tp_comm must be 'peer' or 'nccl', not {tp_comm!r}")
         self.tp_group, self.tp_world, self.tp_rank = tp_group, 1, 0
+        self.peer = None
         if tp_group is not None:
             import torch.distributed as dist
             from .tp import shard_config, shard_getter
@@ -242,6 +248,9 @@ class LeanGemma4:
         self.h2d_bytes = 0
         self.launches = 0
         self.trace = None
+        if tp_group is not None and tp_comm == 'peer':
+            from .tp import PeerExchange
+            self.peer = PeerExchange(tp_group, self.hidden, max(single_max, step_tokens), self.device)
         self.free_bytes = (torch.cuda.mem_get_info(self.device)[0] - (3 << 30)) if self.device.type == 'cuda' else 0
         hd = max(dd for _, dd in self.geom.values())
         qkv_rows = max(l['qkv'].shape[0] for l in self.layers)
@@ -552,6 +561,35 @@ class LeanGemma4:
         self._k('gemm_geglu' if epi == nat.EPI_GEGLU else 'gemm', 'morj_gemm_bf16', a.data_ptr(), a.stride(0), wp,
                 w.stride(0), out.data_ptr(), out.stride(0), M, N, K, epi, self._stream(), flops=2 * M * N * K)
 
+    def _peer_site(self, a, w, mode, n, w_a, scalar, w_b, has_next, push_x):
+        """Tensor parallelism over peer memory: the row-parallel projection a . w^T delivers its partial tiles to the
+        row blocks' owners, each owner reduces its rows with the post-attention (mode 0) or post-MLP (mode 1)
+        epilogue and pushes the new h rows (x rows too when `push_x`) to every rank, then the stream waits for all
+        of h (`morj_gemm_bf16_peer`, `morj_peer_reduce`, `morj_peer_wait`)."""
+        import ctypes
+        from .tp import partial_target, row_target
+        ex, s = self.peer, self._stream()
+        desc = ctypes.addressof(ex.desc)
+        K, N = a.shape[1], w.shape[0]
+        self._k('gemm', 'morj_gemm_bf16_peer', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), n, N, K, desc,
+                s, flops=2 * n * N * K)
+        ex.sites += 1
+        self._k('tp_reduce', 'morj_peer_reduce', desc, mode, n, w_a.data_ptr(), _ptr(scalar), _ptr(w_b), self.eps,
+                has_next, push_x, partial_target(ex.sites, ex.world, self.hidden), s)
+        self._k('tp_reduce', 'morj_peer_wait', desc, n, row_target(ex.sites), s)
+
+    def _peer_rows(self, n):
+        """The exchange's x and h rows for an n-row step; a larger step than the exchange holds rebuilds it on every
+        rank (all ranks plan the same steps, so they rebuild together)."""
+        if n > self.peer.max_rows:
+            import torch.distributed as dist
+            from .tp import PeerExchange
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.tp_group)
+            self.peer.close()
+            self.peer = PeerExchange(self.tp_group, self.hidden, n, self.device)
+        return self.peer.rows_view('x', n), self.peer.rows_view('h', n)
+
     def _reduce(self, t):
         """Tensor parallelism: sum the row-parallel projection's partial output over the ranks (NCCL all-reduce on
         the current stream); nothing on one GPU."""
@@ -607,8 +645,11 @@ class LeanGemma4:
         dev, bf = self.device, torch.bfloat16
         nb = int(st['n_bidir'])
         n_seg = len(st['qo_indptr']) - 1
-        x = torch.empty(n, H, dtype=bf, device=dev)
-        h = torch.empty(n, H, dtype=bf, device=dev)
+        if self.peer is not None:
+            x, h = self._peer_rows(n)
+        else:
+            x = torch.empty(n, H, dtype=bf, device=dev)
+            h = torch.empty(n, H, dtype=bf, device=dev)
         max_pos = int(np.max(st['positions'])) if n else 0
         for kind in set(self.types):
             self._rope(kind, max_pos)
@@ -646,6 +687,15 @@ class LeanGemma4:
             a_i = attn[:, :hq * d]
             self._attention(q_i, k_pool, v_pool, a_i, t, 'qo', 'kv_indptr_' + kk, 'kv_indices_' + kk, n_seg,
                             nb if kind == 'sliding_attention' else 0, kind, 'work_' + kk, n_work[kk])
+            nxt = self.layers[i + 1]['in_ln'] if i < last else layer['in_ln']
+            if self.peer is not None:
+                # x rows go back to every rank once, after the last full layer (the readout gathers them)
+                final = i == last - 1 if self.prune_last else i == last
+                self._peer_site(a_i, layer['o'], 0, n, layer['post_attn'], None, layer['pre_ff'], 1, 0)
+                self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
+                self._peer_site(act, layer['down'], 1, n, layer['post_ff'], layer['scalar'], nxt, int(i < last),
+                                int(final))
+                continue
             self._gemm(a_i, layer['o'], o)
             self._reduce(o)
             self._k('rows', 'morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_attn'].data_ptr(),
@@ -653,7 +703,6 @@ class LeanGemma4:
             self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
             self._gemm(act, layer['down'], o)
             self._reduce(o)
-            nxt = self.layers[i + 1]['in_ln'] if i < last else layer['in_ln']
             self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_ff'].data_ptr(),
                      layer['scalar'].data_ptr(), nxt.data_ptr(), n, H, eps, int(i < last), s)
         # (no pruning) the readout rows' residual stream

@@ -66,3 +66,102 @@ def shard_getter(top, get, rank, world):
             return cols(t, F)
         return t
     return g
+
+
+# ---- peer-memory exchange (the all-reduce of the row-parallel projections, fused with the epilogues) ------------
+
+MAX_RANKS = 8
+BLOCK = 128
+
+
+def exchange_layout(world, hidden, max_rows):
+    """Byte layout of one rank's exchange allocation: the receive area (`world` slabs of `slab_rows` rows, one per
+    source rank, holding the partial rows of this rank's row blocks), the x and h rows of a whole step, and the two
+    per-block counter arrays. Every region starts on a 256-byte boundary."""
+    max_blocks = max(1, -(-max_rows // BLOCK))
+    slab_rows = -(-max_blocks // world) * BLOCK
+    sizes = dict(recv=world * slab_rows * hidden * 2, x=max_blocks * BLOCK * hidden * 2,
+                 h=max_blocks * BLOCK * hidden * 2, partials=max_blocks * 8, rows=max_blocks * 8)
+    off, layout = 0, {}
+    for name in ('recv', 'x', 'h', 'partials', 'rows'):
+        layout[name] = (off, sizes[name])
+        off += -(-sizes[name] // 256) * 256
+    return dict(max_blocks=max_blocks, slab_rows=slab_rows, regions=layout, nbytes=off)
+
+
+def owner(block, world):
+    """The rank that reduces row block `block`."""
+    return block % world
+
+
+def partial_target(sites, world, hidden):
+    """A block's partial-column counter after `sites` reductions: every rank delivers 4 x hidden columns per block
+    per site (4 epilogue warps of 32 rows, each counting the columns of every tile it stored)."""
+    return sites * world * 4 * hidden
+
+
+def row_target(sites):
+    """A block's row counter after `sites` reductions: its owner pushes 128 rows to every rank per site."""
+    return sites * BLOCK
+
+
+def gather_handles(group, handle):
+    """Every rank's IPC handle bytes, in rank order (a collective over `group`)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    return out
+
+
+class PeerExchange:
+    """This rank's exchange buffers, mapped into every peer (CUDA IPC), and the `morj_peer_t` that describes them.
+
+    Collective: every rank of `group` constructs it with the same arguments. `sites` counts the reductions run so
+    far; every rank runs the same sequence, so the cumulative counter targets agree."""
+
+    def __init__(self, group, hidden, max_rows, device):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _native as nat
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > MAX_RANKS:
+            raise ValueError(f'peer exchange supports up to {MAX_RANKS} ranks')
+        lay = exchange_layout(self.world, hidden, max_rows)
+        self.hidden, self.max_rows = hidden, lay['max_blocks'] * BLOCK
+        self.buf = torch.zeros(lay['nbytes'], dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)  # counters are zero before any peer can signal them
+        handle = ctypes.create_string_buffer(nat.IPC_HANDLE_BYTES)
+        nat.call('morj_ipc_export', self.buf.data_ptr(), handle)
+        handles = gather_handles(group, handle.raw)
+        self.bases, self._opened = [], []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                self.bases.append(self.buf.data_ptr())
+                continue
+            ptr = ctypes.c_void_p()
+            nat.call('morj_ipc_import', hb, ctypes.byref(ptr))
+            self.bases.append(ptr.value)
+            self._opened.append((ptr.value, hb))
+        d = nat.PeerDesc()
+        d.world, d.rank, d.max_blocks, d.hidden, d.slab_rows = (self.world, self.rank, lay['max_blocks'], hidden,
+                                                                lay['slab_rows'])
+        for r, base in enumerate(self.bases):
+            for name in ('recv', 'x', 'h', 'partials', 'rows'):
+                getattr(d, name)[r] = base + lay['regions'][name][0]
+        self.desc = d
+        self.regions = lay['regions']
+        self.sites = 0
+        dist.barrier(group=group)
+
+    def rows_view(self, name, n):
+        """This rank's x or h rows [n, hidden] (BF16) inside the exchange allocation."""
+        import torch
+        off, _ = self.regions[name]
+        return self.buf[off:off + n * self.hidden * 2].view(torch.bfloat16).view(n, self.hidden)
+
+    def close(self):
+        from . import _native as nat
+        for ptr, hb in self._opened:
+            nat.call('morj_ipc_close', ptr, hb)
+        self._opened = []

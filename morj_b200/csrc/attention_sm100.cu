@@ -5,12 +5,18 @@
 //   warp 0      K loader: the Q tile (TMA), then each 64-key chunk's K rows into a two-deep ring: one TMA tile load
 //               per head-dim half when the chunk's pool slots are contiguous (tree nodes own contiguous slot runs;
 //               pages hold 64 slots), a cp.async row gather otherwise
-//   warp 1      MMA issuer (one thread): S_c = Q K_c^T into one of two TMEM score buffers, then O += P_{c-1} V_{c-1}
-//               into the TMEM output, so the tensor cores compute chunk c+1's scores while the softmax works on c
+//   warp 1      MMA issuer (one thread): S_c = Q K_c^T into TMEM buffer c % 2, and O += P_c V_c with P read from
+//               TMEM, so the tensor cores compute chunk c+1's scores while the softmax works on c
 //   warp 2      V loader: the same for V, on its own ring (K of chunk c+2 is fetched as soon as S_c is done)
 //   warps 4-7   softmax (thread = row): tree mask (bottom-right causal bound, sliding window, image-block rule), online
 //               softmax in FP32 with a lazily rescaled running maximum (O in TMEM is rescaled only when a row's
-//               maximum grows by more than 2^8), P as BF16 to shared memory, and the final O / l store
+//               maximum grows by more than 2^8), P as BF16 written over its own scores in TMEM, and the final O / l
+//               store
+// P never leaves TMEM: chunk c's P is packed over the first half of S_c's columns and consumed there by the PV MMA, so
+// two score buffers double-buffer P too. S_{c+2} is issued into buffer c % 2 right after P_c V_c: the MMAs of one
+// thread run in issue order, so the PV reads P_c before the next QK^T overwrites it. The same ordering frees the K
+// and V buffers: a loader reuses a K buffer once S_{c-2} is complete and a V buffer once P_{c-2} V_{c-2} is, and the
+// MMA issuer posts two commits per chunk (S_c complete, P_c V_c complete).
 // V is read as an N-major operand, so one shared-memory layout serves K (for QK^T) and V (for PV). The key range of a
 // tile is cut to what its queries can see, so a sliding layer's long prefix costs O(window) per tile.
 #include <algorithm>
@@ -25,7 +31,7 @@ namespace attn {
 constexpr int ROWS = 128;
 constexpr int BN = 64;
 constexpr int THREADS = 256;
-constexpr int TMEM_COLS = 256;  // S buffers at columns [0, 64) and [64, 128), O at [128, 128 + D)
+constexpr int TMEM_COLS = 256;  // S/P buffers at columns [0, 64) and [64, 128), O at [128, 128 + D)
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_LOG2 = 8.0f;  // rescale O only when a row maximum grows by more than 2^8
 
@@ -33,14 +39,12 @@ template <int D>
 struct Smem {
   static constexpr int Q_BYTES = ROWS * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = ROWS * BN * 2;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;       // 2 buffers
   static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;  // 2 buffers
-  static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  // barriers (8 B each): q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full, o_done,
-  // done; then the TMEM slot and the abort flag. The dynamic shared window starts 1024-byte aligned (checked in the
+  static constexpr int BAR_OFF = V_OFF + 2 * KV_BYTES;
+  // barriers (8 B each): q_full, k_full[2], v_full[2], (2 x 2 unused), s_full[2], p_full[2], pv_done[2], done; then
+  // the TMEM slot and the abort flag. The dynamic shared window starts 1024-byte aligned (checked in the
   // kernel), so two CTAs fit an SM.
   static constexpr int TOTAL = BAR_OFF + 160;
 };
@@ -127,8 +131,8 @@ __global__ void __launch_bounds__(THREADS, 2)
     return;
   }
   const uint32_t bar0 = sbase + L::BAR_OFF;
-  const uint32_t q_full = bar0, k_full = bar0 + 8, v_full = bar0 + 24, k_empty = bar0 + 40, v_empty = bar0 + 56;
-  const uint32_t s_full = bar0 + 72, s_free = bar0 + 88, p_full = bar0 + 104, o_done = bar0 + 112, done = bar0 + 120;
+  const uint32_t q_full = bar0, k_full = bar0 + 8, v_full = bar0 + 24;
+  const uint32_t s_full = bar0 + 72, p_full = bar0 + 88, pv_done = bar0 + 104, done = bar0 + 120;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 128);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 132);
 
@@ -166,13 +170,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     for (int b = 0; b < 2; ++b) {
       mbar_init(k_full + 8 * b, 1);
       mbar_init(v_full + 8 * b, 1);
-      mbar_init(k_empty + 8 * b, 1);
-      mbar_init(v_empty + 8 * b, 1);
       mbar_init(s_full + 8 * b, 1);
-      mbar_init(s_free + 8 * b, 4);
+      mbar_init(p_full + 8 * b, 4);  // one arrival per softmax warp
+      mbar_init(pv_done + 8 * b, 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
     mbar_init(done, 1);
     *abort = 0;
     fence_mbar_init();
@@ -200,7 +201,8 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
     if (!is_k && lane == 0) tma_prefetch(&v_map);
     const uint32_t base = sbase + (is_k ? L::K_OFF : L::V_OFF);
-    const uint32_t full = is_k ? k_full : v_full, empty = is_k ? k_empty : v_empty;
+    // a K buffer is free once the scores of the chunk two back are complete, a V buffer once its PV is
+    const uint32_t full = is_k ? k_full : v_full, empty = is_k ? s_full : pv_done;
     for (int c = 0; c < n_chunks; ++c) {
       const int b = c & 1;
       if (c >= 2 && !warp_wait(empty + 8 * b, ((c >> 1) - 1) & 1, abort)) break;
@@ -213,44 +215,42 @@ __global__ void __launch_bounds__(THREADS, 2)
       constexpr uint32_t IDESC_S = idesc_bf16(ROWS, BN);
       constexpr uint32_t IDESC_O = idesc_bf16(ROWS, D, /*b_mn_major=*/true);
       bool ok = mbar_wait(q_full, 0, abort, kErrTimeoutAttention);
-      auto issue_pv = [&](int j) -> bool {
-        if (!mbar_wait(p_full, j & 1, abort, kErrTimeoutAttention)) return false;
-        if (!mbar_wait(v_full + 8 * (j & 1), (j >> 1) & 1, abort, kErrTimeoutAttention)) return false;
-        tc_fence_after();
-        const uint32_t v_s = sbase + L::V_OFF + (j & 1) * L::KV_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t pa = sbase + L::P_OFF + kk * 32;
-          const uint32_t vb = v_s + kk * 2048;
-          umma_bf16(tmem + 128, sw128_desc(pa), sw128_desc(vb, BN * 128), IDESC_O, (j | kk) != 0);
-        }
-        umma_commit(o_done);
-        umma_commit(v_empty + 8 * (j & 1));
-        return true;
-      };
-      for (int c = 0; c < n_chunks && ok; ++c) {
+      // operand descriptors: one per buffer, advanced per 16-deep K step by the byte offset (>> 4)
+      const uint64_t q_desc = sw128_desc(sbase + L::Q_OFF);
+      const uint64_t k_desc0 = sw128_desc(sbase + L::K_OFF), v_desc0 = sw128_desc(sbase + L::V_OFF, BN * 128);
+      constexpr uint64_t KV_STEP = L::KV_BYTES >> 4;
+      auto issue_qk = [&](int c) -> bool {
         const int b = c & 1;
-        if (!mbar_wait(k_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention)) {
-          ok = false;
-          break;
-        }
-        if (c >= 2 && !mbar_wait(s_free + 8 * b, ((c >> 1) - 1) & 1, abort, kErrTimeoutAttention)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(k_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention)) return false;
         tc_fence_after();
-        const uint32_t k_s = sbase + L::K_OFF + b * L::KV_BYTES;
+        const uint64_t k_desc = k_desc0 + b * KV_STEP;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qa = sbase + L::Q_OFF + (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
-          const uint32_t kb = k_s + (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          umma_bf16(tmem + b * BN, sw128_desc(qa), sw128_desc(kb), IDESC_S, kk > 0);
+          const uint32_t qa = ((kk >> 2) * (ROWS * 128) + (kk & 3) * 32) >> 4;
+          const uint32_t kb = ((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4;
+          umma_bf16(tmem + b * BN, q_desc + qa, k_desc + kb, IDESC_S, kk > 0);
         }
         umma_commit(s_full + 8 * b);
-        umma_commit(k_empty + 8 * b);
-        if (c >= 1) ok = issue_pv(c - 1);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      if (ok && n_chunks > 1) ok = issue_qk(1);
+      for (int c = 0; c < n_chunks && ok; ++c) {
+        const int b = c & 1;
+        // O += P_c V_c, P_c from TMEM buffer b (packed BF16 pairs, 8 columns per 16 keys)
+        if (!mbar_wait(p_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention) ||
+            !mbar_wait(v_full + 8 * b, (c >> 1) & 1, abort, kErrTimeoutAttention)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t v_desc = v_desc0 + b * KV_STEP;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_bf16_tmem_a(tmem + 128, tmem + b * BN + kk * 8, v_desc + kk * (2048 >> 4), IDESC_O, (c | kk) != 0);
+        umma_commit(pv_done + 8 * b);
+        if (c + 2 < n_chunks) ok = issue_qk(c + 2);  // in issue order after this PV, which reads P_c first
       }
-      if (ok) issue_pv(n_chunks - 1);
       // TMEM is freed only after every MMA issued here has completed
       umma_commit(done);
       mbar_wait_landed(done, 0);
@@ -276,7 +276,6 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
-    uint8_t* prow = smem + L::P_OFF;
     for (int c = 0; c < n_chunks; ++c) {
       const int b = c & 1;
       if (!warp_wait(s_full + 8 * b, (c >> 1) & 1, abort)) {
@@ -288,9 +287,6 @@ __global__ void __launch_bounds__(THREADS, 2)
       tmem_ld32(t_lane + b * BN, sr[0]);
       tmem_ld32(t_lane + b * BN + 32, sr[1]);
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free + 8 * b);
       const int t0 = t_begin + c * BN;
       // Scores are kept raw; the softmax works in the log2 domain with the scale folded into one FMA per element.
       // Chunks every key of which this row sees (the bulk of a long prefix) skip the per-key mask.
@@ -327,37 +323,30 @@ __global__ void __launch_bounds__(THREADS, 2)
         pk[j / 2] = pack_bf16x2(p0, p1);
       }
       l_run += psum;
-      // P and O are free once the previous chunk's PV has completed
-      if (c >= 1) {
-        if (!warp_wait(o_done, (c - 1) & 1, abort)) {
+      // a rescale of O waits until the previous chunk's PV has completed (the next one needs this chunk's P)
+      if (c >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        if (!warp_wait(pv_done + 8 * (b ^ 1), ((c - 1) >> 1) & 1, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int col = 0; col < D; col += 32) {
-            uint32_t o[32];
-            tmem_ld32(t_lane + 128 + col, o);
-            tmem_wait_ld();
+        for (int col = 0; col < D; col += 32) {
+          uint32_t o[32];
+          tmem_ld32(t_lane + 128 + col, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_lane + 128 + col, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_lane + 128 + col, o);
         }
       }
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint4 v = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-        *reinterpret_cast<uint4*>(prow + sw128_offset(r, cc)) = v;
-      }
-      fence_proxy_async_smem();
+      tmem_st32(t_lane + b * BN, pk);  // P_c over the first 32 columns of S_c
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full + 8 * b);
     }
-    if (ok && warp_wait(o_done, (n_chunks - 1) & 1, abort)) {
+    if (ok && warp_wait(pv_done + 8 * ((n_chunks - 1) & 1), ((n_chunks - 1) >> 1) & 1, abort)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       __nv_bfloat16* dst = out + ((size_t)(sg.q_start + qi) * hq + h * G + r % G) * D;

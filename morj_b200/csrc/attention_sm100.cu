@@ -290,20 +290,24 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int t0 = t_begin + c * BN;
       // Scores are kept raw; the softmax works in the log2 domain with the scale folded into one FMA per element.
       // Chunks every key of which this row sees (the bulk of a long prefix) skip the per-key mask.
+      // (the row maximum and sum run over 8 independent partials: short dependency chains)
       const bool full = t0 >= lo && t0 + BN - 1 <= hi;
-      float mx = -INFINITY;
+      float m8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
       if (__all_sync(0xffffffffu, full)) {
 #pragma unroll
-        for (int j = 0; j < BN; ++j) mx = fmaxf(mx, __uint_as_float(sr[j >> 5][j & 31]));
+        for (int j = 0; j < BN; ++j) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(sr[j >> 5][j & 31]));
       } else {
 #pragma unroll
         for (int j = 0; j < BN; ++j) {
           const int t = t0 + j;
           const float v = (t >= lo && t <= hi) ? __uint_as_float(sr[j >> 5][j & 31]) : -INFINITY;
           sr[j >> 5][j & 31] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
+          m8[j & 7] = fmaxf(m8[j & 7], v);
         }
       }
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= scale_log2;  // scale > 0: the maximum of the scaled scores
       float alpha = 1.f;
       if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
@@ -313,16 +317,18 @@ __global__ void __launch_bounds__(THREADS, 2)
       l_run *= alpha;
       // exp2(-inf) = 0 for masked keys; a row with no visible key yet keeps m_used = -inf and p = 0
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-      float psum = 0.f;
+      float s8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int j = 0; j < BN; j += 2) {
         const float p0 = fast_exp2(fmaf(__uint_as_float(sr[j >> 5][j & 31]), scale_log2, neg_m));
         const float p1 = fast_exp2(fmaf(__uint_as_float(sr[(j + 1) >> 5][(j + 1) & 31]), scale_log2, neg_m));
-        psum += p0 + p1;
+        s8[(j >> 1) & 7] += p0 + p1;
         pk[j / 2] = pack_bf16x2(p0, p1);
       }
-      l_run += psum;
+      l_run += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       // a rescale of O waits until the previous chunk's PV has completed (the next one needs this chunk's P)
       if (c >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
         if (!warp_wait(pv_done + 8 * (b ^ 1), ((c - 1) >> 1) & 1, abort)) {

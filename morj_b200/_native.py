@@ -54,8 +54,8 @@ MAX_RANKS = 8
 
 class PeerDesc(ctypes.Structure):
     """`morj_peer_t`: the exchange buffers of every rank of a tensor-parallel group, as this process sees them."""
-    _fields_ = [('world', I), ('rank', I), ('max_blocks', I), ('hidden', I), ('slab_rows', I), ('pad_', I),
-                ('recv', P * MAX_RANKS), ('x', P * MAX_RANKS), ('h', P * MAX_RANKS),
+    _fields_ = [('world', I), ('rank', I), ('max_blocks', I), ('hidden', I),
+                ('part', P * MAX_RANKS), ('x', P * MAX_RANKS), ('h', P * MAX_RANKS),
                 ('partials', P * MAX_RANKS), ('rows', P * MAX_RANKS)]
 
 

@@ -24,15 +24,13 @@ constexpr int GROUP_M = 16;
 
 // Tile width BN (a multiple of 16, at most 256): the host picks it per shape so the tile count fills whole waves of
 // the SMs; the stage ring is as deep as shared memory allows.
-// EXTRA: shared memory for the epilogue's row staging (the partial-delivery epilogue), after the barriers.
-template <int BN, int EXTRA = 0>
+template <int BN>
 struct Cfg {
   static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "tile width");
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES =
-      (220 * 1024 - EXTRA) / STAGE_BYTES > 6 ? 6 : (220 * 1024 - EXTRA) / STAGE_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EXTRA;
+  static constexpr int STAGES = (220 * 1024) / STAGE_BYTES > 6 ? 6 : (220 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
 };
 
@@ -56,18 +54,18 @@ struct QkvEpi {
   __nv_bfloat16* v_pool;
 };
 
-// Operands of the partial-delivery epilogue (tensor parallelism over peer memory): row block b of the output goes
-// to rank b % world's receive area, slab `rank`, and the delivered columns are counted on that rank's counter b.
+// Operands of the partial epilogue (tensor parallelism over peer memory): the output rows go to this rank's part
+// buffer and the columns written for row block b are counted on the counter b of its owner, rank b % world.
 constexpr int EPI_PEER = 4;
-constexpr int PEER_STAGING = 4 * 4096;  // per epilogue warp: 32 rows x 64 BF16 columns
 struct PeerEpi {
-  __nv_bfloat16* recv[MORJ_MAX_RANKS];
+  __nv_bfloat16* part;
   unsigned long long* partials[MORJ_MAX_RANKS];
-  int world, rank, slab_rows;
+  int world;
 };
 
-MORJ_DEV void red_release_sys_add(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// (after a system fence by every lane and a warp barrier, which order the warp's stores before it)
+MORJ_DEV void red_relaxed_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 MORJ_DEV void store32_bf16(__nv_bfloat16* dst, const float (&v)[32]) {
@@ -222,61 +220,26 @@ MORJ_DEV void store_row(uint32_t tacc, __nv_bfloat16* crow, int n_blk, bool row_
   }
 }
 
-// Partial-delivery epilogue: this warp's 32 rows of the tile go to the row block's owner (over NVLink unless the
-// owner is this rank). Each 64-column slice is staged in shared memory (4 KB per warp, 16-byte units XOR-swizzled by
-// row) and written out as whole 128-byte row segments, four rows per warp store. Once the tile's rows are out the
-// warp counts the tile's columns on the owner's counter (`peer_arrive`: system fence, then a release add); the
-// counter and the count are returned for that. Row blocks wholly past M (the pair kernel's padding) neither store
-// nor count.
+// Partial epilogue: this thread's row of the tile goes to this rank's part buffer (the STORE epilogue's stores);
+// the tile's column count for the row block's owner is returned, to be posted by `peer_arrive`. Row blocks wholly
+// past M (the pair kernel's padding) neither store nor count.
 template <int BN>
-MORJ_DEV void epilogue_peer(uint32_t tacc, int row, int n_blk, int M, int N, const PeerEpi& pe, int lane,
-                            uint4* stage, unsigned long long** count, unsigned long long* cols) {
+MORJ_DEV void epilogue_peer(uint32_t tacc, int row, int n_blk, int M, int N, const PeerEpi& pe,
+                            unsigned long long*& count, unsigned long long& cols) {
   const int blk = row / 128;
   if (blk * 128 >= M) return;
-  const int owner = blk % pe.world;
-  const int row0 = row - lane;  // the warp's first row
-  const size_t local0 = (size_t)(blk / pe.world) * 128 + (row0 & 127);
-  __nv_bfloat16* base = pe.recv[owner] + ((size_t)pe.rank * pe.slab_rows + local0) * N;
-  const int lim = min(N, (n_blk + 1) * BN);
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 64) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t r[32];
-      tmem_ld32(tacc + c + 32 * half, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        uint4 pk;
-        pk.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-        pk.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-        pk.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-        pk.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-        stage[lane * 8 + ((half * 4 + v) ^ (lane & 7))] = pk;
-      }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int idx = it * 32 + lane;
-      const int rr = idx >> 3, chunk = idx & 7;
-      const int col = n_blk * BN + c + chunk * 8;
-      if (row0 + rr < M && col < lim)
-        *reinterpret_cast<uint4*>(base + (size_t)rr * N + col) = stage[rr * 8 + (chunk ^ (rr & 7))];
-    }
-    __syncwarp();
-  }
-  *count = pe.partials[owner] + blk;
-  *cols = (unsigned long long)(lim - n_blk * BN);
+  store_row<BN>(tacc, pe.part + (size_t)row * N, n_blk, row < M, N);
+  count = pe.partials[blk % pe.world] + blk;
+  cols = (unsigned long long)(min(N, (n_blk + 1) * BN) - n_blk * BN);
 }
 
-// The arrival of a delivered tile (deferred to the warp's next accumulator wait, where the system fence's round trip
-// is hidden under the main loop): every lane's stores are visible system-wide before lane 0's release add.
+// The arrival of a written tile (deferred to the warp's next accumulator wait, where the system fence's round trip
+// is hidden under the main loop): every lane's stores are ordered system-wide before lane 0's add.
 MORJ_DEV void peer_arrive(unsigned long long*& count, unsigned long long cols, int lane) {
   if (count == nullptr) return;
   __threadfence_system();
   __syncwarp();
-  if (lane == 0) red_release_sys_add(count, cols);
+  if (lane == 0) red_relaxed_sys_add(count, cols);
   count = nullptr;
 }
 
@@ -323,7 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe,
                 const PeerEpi pe) {
-  using C_ = Cfg<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
+  using C_ = Cfg<BN>;
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -462,9 +425,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
         epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
       } else if constexpr (EPI == EPI_PEER) {
-        epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, lane,
-                          reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256 + quarter * 4096), &pend,
-                          &pend_cols);
+        epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, pend, pend_cols);
       } else {
         epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
       }
@@ -493,14 +454,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 // half of the B tile per k-block, so the L2-to-shared-memory traffic per FLOP drops by a third against the one-CTA
 // kernel. The epilogues are the one-CTA kernel's (each CTA drains its own 128 rows).
 // ---------------------------------------------------------------------------------------------------------------
-template <int BN, int EXTRA = 0>
+template <int BN>
 struct Cfg2 {
   static_assert(BN % 32 == 0 || BN % 16 == 0, "tile width");
   static constexpr int B_HALF_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_HALF_BYTES;
-  static constexpr int STAGES =
-      (200 * 1024 - EXTRA) / STAGE_BYTES > 8 ? 8 : (200 * 1024 - EXTRA) / STAGE_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EXTRA;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN);
 };
 
@@ -509,7 +469,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                  __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe,
                  const PeerEpi pe) {
-  using C_ = Cfg2<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
+  using C_ = Cfg2<BN>;
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -654,9 +614,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
         epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
       } else if constexpr (EPI == EPI_PEER) {
-        epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, lane,
-                          reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256 + quarter * 4096), &pend,
-                          &pend_cols);
+        epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, pend, pend_cols);
       } else {
         epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
       }
@@ -743,7 +701,7 @@ static int make_map(CUtensorMap* map, const void* ptr, long long rows, long long
 template <int EPI, int BN>
 static int launch(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
                   int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}, const PeerEpi& pe = PeerEpi{}) {
-  using C_ = Cfg<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
+  using C_ = Cfg<BN>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -766,7 +724,7 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
 template <int EPI, int BN>
 static int launch2(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
                    int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}, const PeerEpi& pe = PeerEpi{}) {
-  using C_ = Cfg2<BN, EPI == EPI_PEER ? PEER_STAGING : 0>;
+  using C_ = Cfg2<BN>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -875,8 +833,7 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
   if (!A || !B || !peer || M < 0 || N <= 0 || K <= 0)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: bad pointers or sizes (M=%d N=%d K=%d)", M, N, K);
   if (peer->world < 1 || peer->world > MORJ_MAX_RANKS || peer->rank < 0 || peer->rank >= peer->world ||
-      N != peer->hidden || M > peer->max_blocks * 128 ||
-      peer->slab_rows < ((peer->max_blocks + peer->world - 1) / peer->world) * 128)
+      N != peer->hidden || M > peer->max_blocks * 128)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: exchange buffers do not fit (M=%d N=%d)", M, N);
   if (N % 16 || K % 8 || lda % 8 || ldb % 8 || lda < K || ldb < K)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: N % 16, K and leading dimensions % 8 required");
@@ -884,17 +841,17 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: pointers must be 16-byte aligned");
   gemm::PeerEpi pe{};
   for (int r = 0; r < peer->world; ++r) {
-    if (!peer->recv[r] || !peer->partials[r] || (reinterpret_cast<uintptr_t>(peer->recv[r]) & 15))
-      return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's buffers are missing or unaligned", r);
-    pe.recv[r] = reinterpret_cast<__nv_bfloat16*>(peer->recv[r]);
+    if (!peer->partials[r] || (reinterpret_cast<uintptr_t>(peer->partials[r]) & 7))
+      return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's counters are missing or unaligned", r);
     pe.partials[r] = peer->partials[r];
   }
+  if (!peer->part[peer->rank] || (reinterpret_cast<uintptr_t>(peer->part[peer->rank]) & 15))
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: part buffer missing or unaligned");
+  pe.part = reinterpret_cast<__nv_bfloat16*>(peer->part[peer->rank]);
   pe.world = peer->world;
-  pe.rank = peer->rank;
-  pe.slab_rows = peer->slab_rows;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   static const int cand[] = {256, 208, 192, 128};
-  const gemm::Choice c = gemm::pick(M, N, cand, 4, 0);
+  const gemm::Choice c = gemm::pick(M, N, cand, 4, 0);  // (the widths the STORE path picks for these shapes)
   const gemm::QkvEpi qe{};
 #define MORJ_PEER_CASE(W)                                                                                        \
   case W:                                                                                                        \

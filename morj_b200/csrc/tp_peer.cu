@@ -1,12 +1,13 @@
 // Tensor parallelism over peer memory: the owner-side reduction of the row-parallel O / down projections and the
 // hand-back of the reduced rows, replacing an NCCL all-reduce followed by replicated epilogues.
 //
-// Row block b (128 rows) belongs to rank b % world. The row-parallel GEMM (morj_gemm_bf16_peer) has already stored
-// every rank's BF16 partial of block b into the owner's receive area and counted the delivered columns on the
-// owner's counter. Here the owner
+// Row block b (128 rows) belongs to rank b % world. Every rank's row-parallel GEMM (morj_gemm_bf16_peer) has stored
+// its BF16 partial rows in its own part buffer and counted the columns of block b on the owner's counter. Here the
+// owner
 //   1. waits (one thread per CTA, acquire at system scope, bounded) until block b's counter holds every rank's
 //      columns for this site,
-//   2. sums the partials in rank order in FP32 and rounds to BF16,
+//   2. reads block b's partial rows from every rank (NVLink loads from the peers' part buffers), sums them in rank
+//      order in FP32 and rounds to BF16,
 //   3. applies the post-attention or post-MLP epilogue (the math of morj_attn_epilogue / morj_mlp_epilogue) to its
 //      rows, and
 //   4. stores the new h rows (and x rows, when asked) into every rank's buffers over NVLink, then counts one row on
@@ -78,11 +79,9 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
   __syncthreads();
   if (!ok_s) return;  // the peers' waits for this block's rows run out and report too
   const float sc = MODE == 1 ? __bfloat162float(scalar[0]) : 1.f;
-  const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(p.recv[rank]);
   for (int j = 0; j < RED_ROWS; ++j) {
     const int row = blk * 128 + sub + j;
     if (row >= n) break;
-    const size_t local = (size_t)(blk / world) * 128 + sub + j;
     __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(p.x[rank]) + (size_t)row * H;
     float ov[VPT][8];
     float ss = 0.f;
@@ -94,7 +93,7 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
         for (int e = 0; e < 8; ++e) ov[k][e] = 0.f;
         for (int src = 0; src < world; ++src) {
           float pv[8];
-          load8(recv + ((size_t)src * p.slab_rows + local) * H + c, pv);
+          load8(reinterpret_cast<const __nv_bfloat16*>(p.part[src]) + (size_t)row * H + c, pv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) ov[k][e] += pv[e];
         }
@@ -154,11 +153,11 @@ __global__ void __launch_bounds__(ROW_THREADS) wait_kernel(const unsigned long l
 
 static int check_peer(const morj_peer_t* p, const char* who) {
   if (!p || p->world < 1 || p->world > MORJ_MAX_RANKS || p->rank < 0 || p->rank >= p->world || p->max_blocks <= 0 ||
-      p->hidden <= 0 || p->hidden % 8 || p->slab_rows < ((p->max_blocks + p->world - 1) / p->world) * 128)
+      p->hidden <= 0 || p->hidden % 8)
     return set_error(MORJ_ERR_ARG, "%s: bad exchange description", who);
   for (int r = 0; r < p->world; ++r)
-    if (!p->recv[r] || !p->x[r] || !p->h[r] || !p->partials[r] || !p->rows[r] ||
-        ((reinterpret_cast<uintptr_t>(p->recv[r]) | reinterpret_cast<uintptr_t>(p->x[r]) |
+    if (!p->part[r] || !p->x[r] || !p->h[r] || !p->partials[r] || !p->rows[r] ||
+        ((reinterpret_cast<uintptr_t>(p->part[r]) | reinterpret_cast<uintptr_t>(p->x[r]) |
           reinterpret_cast<uintptr_t>(p->h[r])) & 15) ||
         ((reinterpret_cast<uintptr_t>(p->partials[r]) | reinterpret_cast<uintptr_t>(p->rows[r])) & 7))
       return set_error(MORJ_ERR_ARG, "%s: rank %d's buffers are missing or unaligned", who, r);

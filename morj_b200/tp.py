@@ -75,18 +75,17 @@ BLOCK = 128
 
 
 def exchange_layout(world, hidden, max_rows):
-    """Byte layout of one rank's exchange allocation: the receive area (`world` slabs of `slab_rows` rows, one per
-    source rank, holding the partial rows of this rank's row blocks), the x and h rows of a whole step, and the two
-    per-block counter arrays. Every region starts on a 256-byte boundary."""
+    """Byte layout of one rank's exchange allocation: its partial rows of a row-parallel projection (read by the row
+    blocks' owners), the x and h rows of a whole step, and the two per-block counter arrays. Every region starts on
+    a 256-byte boundary."""
     max_blocks = max(1, -(-max_rows // BLOCK))
-    slab_rows = -(-max_blocks // world) * BLOCK
-    sizes = dict(recv=world * slab_rows * hidden * 2, x=max_blocks * BLOCK * hidden * 2,
-                 h=max_blocks * BLOCK * hidden * 2, partials=max_blocks * 8, rows=max_blocks * 8)
+    rows = max_blocks * BLOCK * hidden * 2
+    sizes = dict(part=rows, x=rows, h=rows, partials=max_blocks * 8, rows=max_blocks * 8)
     off, layout = 0, {}
-    for name in ('recv', 'x', 'h', 'partials', 'rows'):
+    for name in ('part', 'x', 'h', 'partials', 'rows'):
         layout[name] = (off, sizes[name])
         off += -(-sizes[name] // 256) * 256
-    return dict(max_blocks=max_blocks, slab_rows=slab_rows, regions=layout, nbytes=off)
+    return dict(max_blocks=max_blocks, regions=layout, nbytes=off)
 
 
 def owner(block, world):
@@ -144,10 +143,9 @@ class PeerExchange:
             self.bases.append(ptr.value)
             self._opened.append((ptr.value, hb))
         d = nat.PeerDesc()
-        d.world, d.rank, d.max_blocks, d.hidden, d.slab_rows = (self.world, self.rank, lay['max_blocks'], hidden,
-                                                                lay['slab_rows'])
+        d.world, d.rank, d.max_blocks, d.hidden = self.world, self.rank, lay['max_blocks'], hidden
         for r, base in enumerate(self.bases):
-            for name in ('recv', 'x', 'h', 'partials', 'rows'):
+            for name in ('part', 'x', 'h', 'partials', 'rows'):
                 getattr(d, name)[r] = base + lay['regions'][name][0]
         self.desc = d
         self.regions = lay['regions']

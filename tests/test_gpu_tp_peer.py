@@ -30,8 +30,7 @@ class Group:
         self.descs = []
         for r in range(world):
             d = nat.PeerDesc()
-            d.world, d.rank, d.max_blocks, d.hidden, d.slab_rows = (world, r, self.lay['max_blocks'], hidden,
-                                                                    self.lay['slab_rows'])
+            d.world, d.rank, d.max_blocks, d.hidden = world, r, self.lay['max_blocks'], hidden
             for q in range(world):
                 for name, (off, _) in self.lay['regions'].items():
                     getattr(d, name)[q] = self.bufs[q].data_ptr() + off
@@ -43,17 +42,8 @@ class Group:
         return self.bufs[r][off:off + rows * self.hidden * 2].view(torch.bfloat16).view(rows, self.hidden)
 
     def delivered(self, n):
-        """The partial rows every rank delivered for rows [0, n): [world, n, hidden], read from the owners' areas."""
-        slab = self.lay['slab_rows']
-        out = torch.empty(self.world, n, self.hidden, dtype=torch.bfloat16, device=DEV)
-        for row in range(0, n, BLOCK):
-            b = row // BLOCK
-            o = owner(b, self.world)
-            recv = self.region(o, 'recv', self.world * slab).view(self.world, slab, self.hidden)
-            lr = (b // self.world) * BLOCK
-            m = min(BLOCK, n - row)
-            out[:, row:row + m] = recv[:, lr:lr + m]
-        return out
+        """Every rank's partial rows [0, n): [world, n, hidden], read from their part buffers."""
+        return torch.stack([self.region(r, 'part', n) for r in range(self.world)])
 
     def site(self, a, w, mode, n, w_a, scalar, w_b, has_next, push_x):
         s = stream()
@@ -149,6 +139,6 @@ def test_peer_arguments_are_checked():
         nat.call('morj_gemm_bf16_peer', a.data_ptr(), 64, a.data_ptr(), 64, 300, 256, 64, d, stream())
     with pytest.raises(ValueError):  # N must be the exchange's hidden size
         nat.call('morj_gemm_bf16_peer', a.data_ptr(), 64, a.data_ptr(), 64, 200, 128, 64, d, stream())
-    grp.descs[0].recv[1] = None
+    grp.descs[0].part[1] = None
     with pytest.raises(ValueError):
         nat.call('morj_peer_wait', d, 10, 0, stream())

@@ -15,15 +15,13 @@ from morj_b200.tp import BLOCK, exchange_layout, owner, partial_target, row_targ
 @pytest.mark.parametrize('hidden,max_rows', [(256, 1), (256, 1000), (5376, 16384), (5376, 16385)])
 def test_exchange_layout(world, hidden, max_rows):
     lay = exchange_layout(world, hidden, max_rows)
-    mb, slab = lay['max_blocks'], lay['slab_rows']
-    assert mb * BLOCK >= max_rows and slab % BLOCK == 0
-    # every owner's blocks fit its slab: rank r owns ceil((mb - r) / world) blocks
-    assert all(-(-(mb - r) // world) * BLOCK <= slab for r in range(world))
+    mb = lay['max_blocks']
+    assert mb * BLOCK >= max_rows
     regions = sorted(lay['regions'].values())
     for (o1, s1), (o2, _) in zip(regions, regions[1:]):
         assert o1 % 256 == 0 and o1 + s1 <= o2
     assert regions[-1][0] + regions[-1][1] <= lay['nbytes']
-    assert lay['regions']['recv'][1] == world * slab * hidden * 2
+    assert lay['regions']['part'][1] == lay['regions']['x'][1] == lay['regions']['h'][1] == mb * BLOCK * hidden * 2
     assert lay['regions']['partials'][1] == mb * 8 == lay['regions']['rows'][1]
 
 

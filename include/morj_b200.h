@@ -23,6 +23,9 @@
  *                             lean_core.py:558-561 with the norm of 692/736
  *   morj_gather_rows          x[rows] / hn[rows] gathers, lean_core.py:692,708,730
  *   morj_scatter_rows         K/V head copy into pool slots (_fill_head), lean_core.py:594-597
+ *   morj_tree_build / morj_tree_layout / morj_plan_pass
+ *                             the host planner: Tree.__init__ and Tree.plan_pass (with _depth_first, the step cut and
+ *                             the liveness slot allocator), lean_core.py:38-83, 120-231
  */
 #ifndef MORJ_B200_H
 #define MORJ_B200_H
@@ -38,6 +41,7 @@ extern "C" {
 #define MORJ_ERR_OOM 3      /* out of device memory (never raised by calls that allocate nothing) */
 #define MORJ_ERR_TIMEOUT 4  /* a kernel's bounded wait ran out (see morj_device_error) */
 #define MORJ_ERR_UNSUPPORTED 5
+#define MORJ_ERR_INTERNAL 6 /* an internal consistency check failed (the reference raises AssertionError there) */
 
 /* GEMM epilogues */
 #define MORJ_EPI_STORE 0 /* C[M,N] = bf16(A[M,K] . B[N,K]^T) */
@@ -198,6 +202,39 @@ int morj_peer_reduce(const morj_peer_t* peer, int mode, int n, const void* w_a, 
 
 /* Hold the stream until every row block below n has reached row_target on this rank's row counters. */
 int morj_peer_wait(const morj_peer_t* peer, int n, unsigned long long row_target, void* stream);
+
+/* ---- host planner (reference Tree, lean_core.py:34-231); host memory only, no CUDA ----------------------------
+ *
+ * morj_tree_build: the radix layout of n_seqs token sequences (tokens concatenated, seq_indptr[n_seqs + 1]); *tree
+ * is an opaque handle, released with morj_tree_free. morj_tree_layout: sizes[3] = {nodes, path entries, node-path
+ * entries}; with non-null arrays it also writes nodes[3 * n] (owner sequence, start depth, end depth; numbered by
+ * start depth, ties by creation), offsets[n + 1], the per-sequence node paths (CSR: path_indptr[n_seqs + 1],
+ * path_ids) and the per-node root paths (CSR: node_path_indptr[n + 1], node_path_ids). */
+int morj_tree_build(const long long* tokens, const long long* seq_indptr, int n_seqs, void** tree);
+int morj_tree_layout(const void* tree, long long* sizes, long long* nodes, long long* offsets, long long* path_indptr,
+                     long long* path_ids, long long* node_path_indptr, long long* node_path_ids);
+void morj_tree_free(void* tree);
+
+/* Plan one pass over the nodes `compute` (in the caller's order) reading out `readout_seqs` (reference
+ * Tree.plan_pass, same arguments): window, single_max, step_tokens, identity (slot = tree offset); prealloc: tree
+ * offsets resident in slots 0.. (the shared head); initial_g/_s: per-kind slot tables of the previous pass
+ * (num_tokens entries, -1 = none; both or neither); pinned_g/_s: offsets never freed; bidir: image-block node ids.
+ * *plan is an opaque handle (morj_plan_free). Errors: MORJ_ERR_ARG (bad input, or a readout token is not computed
+ * in the pass), MORJ_ERR_INTERNAL (a segment reads a token that has no slot).
+ * morj_plan_blob: the plan as int64 values, in order:
+ *   num_tokens, n_steps, cap_g, cap_s, n_readout; slot_of_g[num_tokens]; slot_of_s[num_tokens];
+ *   readout (step, row)[n_readout];
+ *   per step: n_segs, n_rows, n_bidir, n_kv_g, n_kv_s; segs (node, start depth, end depth)[n_segs]; own[n_rows]
+ *   (tree offsets); positions[n_rows]; tokens[n_rows]; qo_indptr[n_segs + 1]; slots_g[n_rows]; slots_s[n_rows];
+ *   kv_indptr_g[n_segs + 1]; kv_indices_g[n_kv_g]; kv_indptr_s[n_segs + 1]; kv_indices_s[n_kv_s].
+ * The pointer stays valid until morj_plan_free. */
+int morj_plan_pass(const void* tree, const long long* compute, int n_compute, const int* readout_seqs, int n_readout,
+                   int window, long long single_max, long long step_tokens, int identity, const long long* prealloc,
+                   long long n_prealloc, const long long* initial_g, const long long* initial_s,
+                   const long long* pinned_g, long long n_pinned_g, const long long* pinned_s, long long n_pinned_s,
+                   const long long* bidir, int n_bidir, void** plan);
+int morj_plan_blob(const void* plan, const long long** data, long long* len);
+void morj_plan_free(void* plan);
 
 #ifdef __cplusplus
 }

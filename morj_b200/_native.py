@@ -11,7 +11,7 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, '_morj_b200.so')
 
-OK, ERR_ARG, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
+OK, ERR_ARG, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_INTERNAL = 0, 1, 2, 3, 4, 5, 6
 EPI_STORE, EPI_GEGLU = 0, 1
 
 _lock = threading.Lock()
@@ -46,7 +46,12 @@ SIGNATURES = {
     'morj_gemm_bf16_peer': [P, LL, P, LL, I, I, I, P, P],
     'morj_peer_reduce': [P, I, I, P, P, P, F, I, I, ctypes.c_ulonglong, P],
     'morj_peer_wait': [P, I, ctypes.c_ulonglong, P],
+    'morj_tree_build': [P, P, I, ctypes.POINTER(P)],
+    'morj_tree_layout': [P, P, P, P, P, P, P, P],
+    'morj_plan_pass': [P, P, I, P, I, I, LL, LL, I, P, LL, P, P, P, LL, P, LL, P, I, ctypes.POINTER(P)],
+    'morj_plan_blob': [P, ctypes.POINTER(ctypes.POINTER(ctypes.c_longlong)), ctypes.POINTER(LL)],
 }
+VOID_SIGNATURES = {'morj_tree_free': [P], 'morj_plan_free': [P]}
 
 IPC_HANDLE_BYTES = 72
 MAX_RANKS = 8
@@ -75,6 +80,10 @@ def lib():
                     fn = getattr(L, name)
                     fn.argtypes = args
                     fn.restype = ctypes.c_int
+                for name, args in VOID_SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.argtypes = args
+                    fn.restype = None
                 L.morj_last_error.argtypes = []
                 L.morj_last_error.restype = ctypes.c_char_p
                 _lib = L
@@ -90,6 +99,8 @@ def check(status, what):
         raise ValueError(text)
     if status == ERR_OOM:
         raise MemoryError(text)
+    if status == ERR_INTERNAL:
+        raise AssertionError(text)
     raise NativeFailure(f'{text} (status {status})')
 
 

@@ -1,4 +1,5 @@
-"""Build the native library `morj_b200/_morj_b200.so` from `morj_b200/csrc/*.cu` for sm_100a (nvcc, in-tree).
+"""Build the native library `morj_b200/_morj_b200.so` from `morj_b200/csrc/*.cu` (device code for sm_100a, nvcc)
+and `morj_b200/csrc/*.cpp` (host code, g++), in-tree.
 
     python -m morj_b200.build [--force] [--verbose]
 
@@ -17,13 +18,15 @@ CSRC = os.path.join(HERE, 'csrc')
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, '_morj_b200.so')
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
+CXX = os.environ.get('CXX', 'g++')
+CXXFLAGS = ['-O3', '-std=c++17', '-fPIC', '-Wall', '-I', os.path.join(ROOT, 'include')]
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 FLAGS = ['-O3', '-lineinfo', '-std=c++17', '-rdc=true', '-Xcompiler', '-fPIC,-O3', '--expt-relaxed-constexpr',
          '-I', os.path.join(ROOT, 'include')]
 
 
 def sources():
-    return sorted(glob.glob(os.path.join(CSRC, '*.cu')))
+    return sorted(glob.glob(os.path.join(CSRC, '*.cu')) + glob.glob(os.path.join(CSRC, '*.cpp')))
 
 
 def headers():
@@ -38,7 +41,7 @@ def stale():
 
 
 def build(force=False, verbose=False):
-    """Compile every .cu to an object (in parallel) and link the shared library; returns its path."""
+    """Compile every source to an object (in parallel) and link the shared library; returns its path."""
     if not force and not stale():
         return LIB
     objdir = os.path.join(HERE, '_build')
@@ -47,9 +50,12 @@ def build(force=False, verbose=False):
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src) + '.o')
         objs.append(obj)
-        cmd = [NVCC, *ARCH, *FLAGS, '-c', src, '-o', obj]
-        if verbose:
-            cmd += ['-Xptxas', '-v']
+        if src.endswith('.cpp'):
+            cmd = [CXX, *CXXFLAGS, '-c', src, '-o', obj]
+        else:
+            cmd = [NVCC, *ARCH, *FLAGS, '-c', src, '-o', obj]
+            if verbose:
+                cmd += ['-Xptxas', '-v']
         procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
     failed = []
     for src, p in procs:

@@ -1,4 +1,4 @@
-"""Token-tree layout and pass planner for the tree-prefill engine (host side, numpy).
+"""Token-tree layout and pass planner for the tree-prefill engine (host side).
 
 A request's sequences (branches) share prefixes. The tree stores every distinct prefix token once: node `i` covers
 depths `[start, end)` of the sequence that first produced them, and owns the tree offsets
@@ -11,26 +11,30 @@ its children. A pass plan cuts the nodes to compute into steps and gives, per st
   `kv_indices[kv_indptr[s]:kv_indptr[s + 1]]` (page size 1), which are its path's tokens in depth order (only the
   last `window` before the segment's first query for sliding layers), bottom-right aligned with its queries.
 
-The plan is bit-exact with the reference planner (`aleria_judge/lean_core.py:34-231`, `Tree`): the same node ids,
-offsets, step cuts, readout rows and slot numbers, because the K/V pools and tree tables it produces are the
-contract the kernels and the request-level retention modes read. The code here is an independent implementation
-of those published rules; `tests/test_tree_golden.py` compares it with fixtures recorded from the reference.
+The layout and the plan are computed by the native planner (`morj_tree_build`, `morj_plan_pass` in
+`morj_b200/csrc/planner.cpp`); this class keeps the reference's Python interface over them. The plan is bit-exact with
+the reference planner (`aleria_judge/lean_core.py:34-231`, `Tree`): the same node ids, offsets, step cuts, readout
+rows and slot numbers, because the K/V pools and tree tables it produces are the contract the kernels and the
+request-level retention modes read. `tests/test_tree_golden.py` compares it with fixtures recorded from the
+reference.
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
+
+from . import _native as nat
 
 KINDS = ('g', 's')
 
 
-def _common_prefix(a: np.ndarray, b: np.ndarray) -> int:
-    """Length of the longest common prefix of two int64 arrays."""
-    n = min(len(a), len(b))
-    if n == 0:
-        return 0
-    neq = a[:n] != b[:n]
-    k = int(np.argmax(neq))
-    return n if not neq[k] else k
+def _ptr(a):
+    return a.ctypes.data if a is not None and a.size else None
+
+
+def _i64(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int64).reshape(-1))
 
 
 class Tree:
@@ -43,52 +47,42 @@ class Tree:
     """
 
     def __init__(self, seqs):
-        self.seqs = [np.asarray(s, dtype=np.int64) for s in seqs]
-        raw: list[list[int]] = []        # creation order: [owner, start, end]
-        members: list[list[int]] = []    # per sequence: creation ids from the root
-        for b, seq in enumerate(self.seqs):
-            # the earlier sequence sharing the longest prefix (first one on ties) and that length
-            donor, shared = -1, 0
-            for j in range(b):
-                c = _common_prefix(seq, self.seqs[j])
-                if c > shared:
-                    donor, shared = j, c
-            route: list[int] = []
-            if donor >= 0:
-                for nid in list(members[donor]):
-                    owner, start, end = raw[nid]
-                    if end <= shared:
-                        route.append(nid)
-                        continue
-                    if start < shared:
-                        # the branch point falls inside this node: keep [start, shared) here and move the rest to a
-                        # new node, which follows it on every path through it
-                        raw.append([owner, shared, end])
-                        tail = len(raw) - 1
-                        raw[nid][2] = shared
-                        for m in members:
-                            if nid in m:
-                                m.insert(m.index(nid) + 1, tail)
-                        route.append(nid)
-                    break
-            if shared < len(seq):
-                raw.append([b, shared, len(seq)])
-                route.append(len(raw) - 1)
-            members.append(route)
-        order = sorted(range(len(raw)), key=lambda i: (raw[i][1], i))
-        new_id = np.empty(len(raw), dtype=np.int64)
-        new_id[np.asarray(order, dtype=np.int64)] = np.arange(len(raw))
-        self.nodes = [raw[i] for i in order]
-        self.paths = [[int(new_id[n]) for n in m] for m in members]
-        lengths = [e - s for _, s, e in self.nodes]
-        self.offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
-        self.num_tokens = int(self.offsets[-1])
-        self.prompt_tokens = sum(len(s) for s in self.seqs)
-        self.node_path = {}
-        for p in self.paths:
-            for i, nid in enumerate(p):
-                if nid not in self.node_path:
-                    self.node_path[nid] = p[:i + 1]
+        self.seqs = [np.asarray(s, dtype=np.int64).reshape(-1) for s in seqs]
+        lens = np.array([len(s) for s in self.seqs], dtype=np.int64)
+        indptr = np.zeros(len(self.seqs) + 1, dtype=np.int64)
+        np.cumsum(lens, out=indptr[1:])
+        tokens = np.ascontiguousarray(np.concatenate(self.seqs)) if self.seqs else np.zeros(0, np.int64)
+        handle = ctypes.c_void_p()
+        nat.call('morj_tree_build', _ptr(tokens), indptr.ctypes.data, len(self.seqs), ctypes.byref(handle))
+        self._handle = handle
+        sizes = np.zeros(3, dtype=np.int64)
+        nat.call('morj_tree_layout', handle, sizes.ctypes.data, None, None, None, None, None, None)
+        n, n_path, n_np = (int(x) for x in sizes)
+        nodes = np.zeros((max(n, 1), 3), dtype=np.int64)
+        offsets = np.zeros(n + 1, dtype=np.int64)
+        path_indptr = np.zeros(len(self.seqs) + 1, dtype=np.int64)
+        path_ids = np.zeros(max(n_path, 1), dtype=np.int64)
+        np_indptr = np.zeros(n + 1, dtype=np.int64)
+        np_ids = np.zeros(max(n_np, 1), dtype=np.int64)
+        nat.call('morj_tree_layout', handle, sizes.ctypes.data, nodes.ctypes.data, offsets.ctypes.data,
+                 path_indptr.ctypes.data, path_ids.ctypes.data, np_indptr.ctypes.data, np_ids.ctypes.data)
+        self.nodes = nodes[:n].tolist()
+        pi, ids = path_indptr.tolist(), path_ids.tolist()
+        self.paths = [ids[pi[b]:pi[b + 1]] for b in range(len(self.seqs))]
+        self.offsets = offsets
+        self.num_tokens = int(offsets[-1])
+        self.prompt_tokens = int(lens.sum())
+        ni, nids = np_indptr.tolist(), np_ids.tolist()
+        self.node_path = {i: nids[ni[i]:ni[i + 1]] for i in range(n) if ni[i + 1] > ni[i]}
+
+    def __del__(self):
+        handle = getattr(self, '_handle', None)
+        if handle is not None and handle.value:
+            try:
+                nat.lib().morj_tree_free(handle)
+            except Exception:  # interpreter shutdown
+                pass
+            self._handle = None
 
     # ---- lookups --------------------------------------------------------------------------------------------------
     def slots(self, nid):
@@ -140,43 +134,6 @@ class Tree:
         return {k: (np.unique(np.concatenate(v)) if v else np.zeros(0, np.int64)) for k, v in keep.items()}
 
     # ---- planning -------------------------------------------------------------------------------------------------
-    def _depth_first(self, compute):
-        """`compute` in depth-first pre-order over the sub-forest it spans, children in ascending id order."""
-        todo = set(compute)
-        kids: dict[int, list[int]] = {}
-        for n in compute:
-            np_ = self.node_path[n]
-            parent = np_[-2] if len(np_) > 1 else -1
-            kids.setdefault(parent if parent in todo else -1, []).append(n)
-        out, stack = [], sorted(kids.get(-1, []), reverse=True)
-        while stack:
-            n = stack.pop()
-            out.append(n)
-            stack.extend(sorted(kids.get(n, []), reverse=True))
-        return out
-
-    def _cut(self, compute, budget, bidir):
-        """Cut the node list into steps of at most `budget` tokens; image blocks (`bidir`) are never split."""
-        steps, cur, room = [], [], budget
-        for n in compute:
-            a, end = self.nodes[n][1], self.nodes[n][2]
-            whole = n in bidir
-            if whole and end - a > room and cur:
-                steps.append(cur)
-                cur, room = [], budget
-            while a < end:
-                take = end - a if whole else min(end - a, room)
-                cur.append((n, a, a + take))
-                a += take
-                room -= take
-                if room <= 0:
-                    steps.append(cur)
-                    cur, room = [], budget
-        if cur:
-            steps.append(cur)
-        # image blocks lead their step: their queries attend without the causal mask in sliding layers
-        return [[s for s in st if s[0] in bidir] + [s for s in st if s[0] not in bidir] for st in steps]
-
     def plan_pass(self, compute, readout_seqs, window, single_max, step_tokens, identity, prealloc=(), initial=None,
                   pinned=None, bidir=frozenset()):
         """Plan one pass over the nodes `compute` (reference `lean_core.py:120-231`; same arguments and result).
@@ -184,95 +141,79 @@ class Tree:
         Returns `dict(steps=[...], cap={kind: slots}, slot_of={kind: offset -> slot}, readout=[(step, row)])`; each
         step is a dict with `segs, own, positions, tokens, n_bidir, qo_indptr, slots, kv_indptr_g, kv_indices_g,
         kv_indptr_s, kv_indices_s`."""
-        compute = list(compute)
-        total = sum(self.span(n) for n in compute)
-        if total > single_max:
-            budget = step_tokens
-            compute = self._depth_first(compute)
-        else:
-            budget = total
-        cuts = self._cut(compute, budget, bidir)
+        comp = _i64(list(compute))
+        ro = np.ascontiguousarray(np.asarray(list(readout_seqs), dtype=np.int32))
+        pre = _i64(prealloc)
+        ini = [_i64(initial[k]) for k in KINDS] if initial is not None else [None, None]
+        for t in ini:
+            if t is not None and len(t) != self.num_tokens:
+                raise ValueError('initial slot tables must cover every tree offset')
+        pin = [_i64(pinned[k]) for k in KINDS] if pinned is not None else [None, None]
+        bid = _i64(sorted(int(n) for n in bidir))
+        handle = ctypes.c_void_p()
+        nat.call('morj_plan_pass', self._handle, _ptr(comp), len(comp), _ptr(ro), len(ro), int(window),
+                 int(single_max), int(step_tokens), int(bool(identity)), _ptr(pre), len(pre),
+                 _ptr(ini[0]) if ini[0] is not None else None, _ptr(ini[1]) if ini[1] is not None else None,
+                 _ptr(pin[0]) if pin[0] is not None else None, len(pin[0]) if pin[0] is not None else 0,
+                 _ptr(pin[1]) if pin[1] is not None else None, len(pin[1]) if pin[1] is not None else 0,
+                 _ptr(bid), len(bid), ctypes.byref(handle))
+        try:
+            data = ctypes.POINTER(ctypes.c_longlong)()
+            n = ctypes.c_longlong()
+            nat.call('morj_plan_blob', handle, ctypes.byref(data), ctypes.byref(n))
+        except BaseException:
+            nat.lib().morj_plan_free(handle)
+            raise
+        # the plan's arrays are views of the native buffer, which lives as long as any of them
+        buf = (ctypes.c_longlong * n.value).from_address(ctypes.addressof(data.contents))
+        buf._owner = _PlanHandle(handle)
+        return _parse_plan(np.frombuffer(buf, dtype=np.int64))
 
-        # readout rows: tree offset -> indices into readout_seqs
-        want: dict[int, list[int]] = {}
-        for i, b in enumerate(readout_seqs):
-            want.setdefault(self.readout_slot(b)[1], []).append(i)
-        readout = [None] * len(readout_seqs)
 
-        last_read = {k: np.full(self.num_tokens, -1) for k in KINDS}
-        steps = []
-        for k, segs in enumerate(cuts):
-            own, pos, toks, lists = [], [], [], {'g': [], 's': []}
-            for n, a, b in segs:
-                owner, sn, _ = self.nodes[n]
-                base = self.offsets[n]
-                ancestors = [self.slots(p) for p in self.node_path[n][:-1]]
-                path = np.concatenate(ancestors + [base + np.arange(0, b - sn)])
-                lists['g'].append(path)
-                lists['s'].append(path[max(0, a - window + 1):])
-                for kind in KINDS:
-                    last_read[kind][lists[kind][-1]] = k
-                own.append(base + np.arange(a - sn, b - sn))
-                pos.append(np.arange(a, b))
-                toks.append(self.seqs[owner][a:b])
-            own = np.concatenate(own)
-            hits = np.flatnonzero(np.isin(own, list(want)))
-            for r in hits:
-                for i in want[int(own[r])]:
-                    readout[i] = (k, int(r))
-            steps.append(dict(segs=segs, own=own, kv=lists, positions=np.concatenate(pos),
-                              tokens=np.concatenate(toks), n_bidir=sum(1 for s in segs if s[0] in bidir),
-                              qo_indptr=np.concatenate([[0], np.cumsum([b - a for _, a, b in segs])])))
-        if any(r is None for r in readout):
-            raise ValueError('a readout token is not computed in this pass')
+class _PlanHandle:
+    """Frees a native plan when the last view of its buffer goes."""
 
-        slot_of, cap = {}, {}
-        for kind in KINDS:
-            if identity:
-                slot_of[kind], cap[kind] = np.arange(self.num_tokens), self.num_tokens
-                continue
-            slot_of[kind], cap[kind] = self._allocate(kind, steps, last_read[kind], prealloc, initial, pinned)
-        for st in steps:
-            st['slots'] = {kind: slot_of[kind][st['own']] for kind in KINDS}
-            for kind in KINDS:
-                idx = [slot_of[kind][x] for x in st['kv'][kind]]
-                for i in idx:
-                    if (i < 0).any():
-                        raise AssertionError('a segment reads a token that has no slot')
-                st['kv_indptr_' + kind] = np.concatenate([[0], np.cumsum([len(i) for i in idx])])
-                st['kv_indices_' + kind] = np.concatenate(idx)
-            del st['kv']
-        return dict(steps=steps, cap=cap, slot_of=slot_of, readout=readout)
+    def __init__(self, handle):
+        self.handle = handle
 
-    def _allocate(self, kind, steps, last_read, prealloc, initial, pinned):
-        """Liveness slot allocator for one kind: computed tokens take the lowest free slots (then new ones on top);
-        with several steps, a slot is freed after the last step that reads its token. Resident tokens (`initial`, or
-        the `prealloc` head) keep their slots; `pinned` offsets are never freed (reference `lean_core.py:198-222`)."""
-        if initial is not None:
-            table = initial[kind].copy()
-        else:
-            table = np.full(self.num_tokens, -1)
-            table[np.asarray(prealloc, dtype=np.int64)] = np.arange(len(prealloc))
-        last = last_read
-        if pinned is not None:
-            last[pinned[kind]] = len(steps)
-        resident = table >= 0
-        top = int(table.max()) + 1 if resident.any() else 0
-        taken = np.zeros(top, dtype=bool)
-        taken[table[resident]] = True
-        free = sorted(np.flatnonzero(~taken).tolist(), reverse=True)   # pop() gives the lowest free slot
-        multi = len(steps) > 1
-        for k, st in enumerate(steps):
-            own = st['own']
-            reuse = min(len(free), len(own))
-            got = [free.pop() for _ in range(reuse)]
-            fresh = top + np.arange(len(own) - reuse)
-            table[own] = np.concatenate([np.asarray(got, dtype=np.int64), fresh])
-            top += len(own) - reuse
-            resident[own] = True
-            if multi:
-                gone = np.flatnonzero(resident & (last <= k))
-                resident[gone] = False
-                free.extend(table[gone].tolist())
-                free.sort(reverse=True)
-        return table, top
+    def __del__(self):
+        try:
+            nat.lib().morj_plan_free(self.handle)
+        except Exception:  # interpreter shutdown
+            pass
+
+
+def _parse_plan(blob):
+    """The plan dict from `morj_plan_blob`'s int64 layout (views into `blob`)."""
+    nt, n_steps, cap_g, cap_s, n_ro = (int(x) for x in blob[:5])
+    p = 5
+    slot_of = {}
+    for k in KINDS:
+        slot_of[k] = blob[p:p + nt]
+        p += nt
+    readout = [tuple(r) for r in blob[p:p + 2 * n_ro].reshape(-1, 2).tolist()]
+    p += 2 * n_ro
+    steps = []
+    for _ in range(n_steps):
+        n_segs, n_rows, n_bidir, n_kv_g, n_kv_s = (int(x) for x in blob[p:p + 5])
+        p += 5
+        segs = [tuple(s) for s in blob[p:p + 3 * n_segs].reshape(-1, 3).tolist()]
+        p += 3 * n_segs
+        st = dict(segs=segs, n_bidir=n_bidir)
+        for key in ('own', 'positions', 'tokens'):
+            st[key] = blob[p:p + n_rows]
+            p += n_rows
+        st['qo_indptr'] = blob[p:p + n_segs + 1]
+        p += n_segs + 1
+        st['slots'] = {}
+        for k in KINDS:
+            st['slots'][k] = blob[p:p + n_rows]
+            p += n_rows
+        for k, n_kv in zip(KINDS, (n_kv_g, n_kv_s)):
+            st['kv_indptr_' + k] = blob[p:p + n_segs + 1]
+            p += n_segs + 1
+            st['kv_indices_' + k] = blob[p:p + n_kv]
+            p += n_kv
+        steps.append(st)
+    assert p == len(blob), 'plan blob layout'
+    return dict(steps=steps, cap={'g': cap_g, 's': cap_s}, slot_of=slot_of, readout=readout)

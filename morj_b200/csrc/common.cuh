@@ -71,13 +71,28 @@ MORJ_DEV bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a waiting thread is suspended (it takes no issue slots from the warps that are
+// working) until the phase completes or about `ns` nanoseconds pass.
+MORJ_DEV bool mbar_test_suspend(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with `parity` to complete. Returns false (after reporting `code` and raising `*abort`) when
-// the wait runs past the limit, or as soon as another thread of the CTA raised `*abort`.
+// the wait runs past the limit, or as soon as another thread of the CTA raised `*abort` (checked every 64 tries;
+// each try suspends for at most 20 us).
 MORJ_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity, 20000)) return true;
     if ((i & 63) == 0) {
       if (*abort) return false;
       if (global_ns() - t0 > kWaitLimitNs) {

@@ -46,6 +46,7 @@ SIGNATURES = {
     'morj_gemm_bf16_peer': [P, LL, P, LL, I, I, I, P, P],
     'morj_peer_reduce': [P, I, I, P, P, P, F, I, I, ctypes.c_ulonglong, P],
     'morj_peer_wait': [P, I, ctypes.c_ulonglong, P],
+    'morj_gemm_norm_epilogue_noalloc': [P, LL, P, LL, I, I, I, I, P, P, P, P, P, F, I, P],
     'morj_tree_build': [P, P, I, ctypes.POINTER(P)],
     'morj_tree_layout': [P, P, P, P, P, P, P, P],
     'morj_plan_pass': [P, P, I, P, I, I, LL, LL, I, P, LL, P, P, P, LL, P, LL, P, I, ctypes.POINTER(P)],

@@ -48,9 +48,10 @@ MORJ_DEV bool wait_at_least(const unsigned long long* p, unsigned long long targ
   }
 }
 
-constexpr int RED_ROWS = 16;  // rows per CTA: one wait, one system fence and one arrival per 16 rows
+constexpr int RED_ROWS = 4;  // rows per CTA (one wait, one system fence and one arrival each): many CTAs keep many
+                             // rows' remote loads in flight
 
-// One CTA per 16 rows of this rank's row blocks below n, plus one last CTA that pads the blocks past n.
+// One CTA per 4 rows of this rank's row blocks below n, plus one last CTA that pads the blocks past n.
 template <int VPT, int MODE>
 __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p, int n,
                                                             const __nv_bfloat16* __restrict__ w_a,

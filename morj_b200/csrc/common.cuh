@@ -268,8 +268,11 @@ MORJ_DEV uint32_t map_shared(uint32_t addr, uint32_t rank) {
 MORJ_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Arrival on a barrier that may live in the peer CTA of the pair. Relaxed: it signals that this warp's reads of the
+// accumulator (completed by tcgen05.wait::ld before it) are done, and orders none of the warp's global stores, which
+// a release at cluster scope would make it wait for.
 MORJ_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA tile load whose completion is counted on an mbarrier that may live in the peer CTA of the pair
 MORJ_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,

@@ -462,8 +462,8 @@ def main():
             dtype='bf16',
             data='synthetic (seeded random-init weights N(0, 0.02), uniform token ids)',
             config=dict(workload=f'31B-class Gemma-style decoder, {desc}', tokens=tokens,
-                        parallelism=((f'tensor parallel x{world} (O/down partials stored to the row owners over '
-                                      f'NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else
+                        parallelism=((f'tensor parallel x{world} (O/down partial rows read by their row owners '
+                                      f'over NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else
                                       f'tensor parallel x{world} (NCCL all-reduce after O and down)') if tp else
                                      f'replicas x{world} (independent trees, no collective)'),
                         l2='inputs larger than L2 (52 GB of weights streamed per step)',

@@ -204,8 +204,7 @@ int morj_peer_reduce(const morj_peer_t* peer, int mode, int n, const void* w_a, 
 int morj_peer_wait(const morj_peer_t* peer, int n, unsigned long long row_target, void* stream);
 
 /* No counterpart in the reference. For callers that cannot allocate device memory (a process binding this C-ABI
- * from another language that owns only the buffers it passes in, or code running while its stream is captured,
- * where cudaMalloc is not allowed): the one-rank row-parallel projection and norm epilogue, C = A . B^T
+ * from another language that owns only the buffers it passes in and may not call cudaMalloc itself): the one-rank row-parallel projection and norm epilogue, C = A . B^T
  * ([M, N] BF16, N = H) followed by morj_peer_reduce's epilogue on every row (mode 0: post-attention, w_a = post_attn,
  * w_b = pre_ff, h required; mode 1: post-MLP, w_a = post_ff, scalar, w_b = next input norm, has_next). x is updated
  * in place, h written. Its scratch (the C rows and the block counters) is a fixed array inside the library, 8 MiB

@@ -3,8 +3,8 @@
 // morj_gemm_bf16_peer followed by morj_peer_reduce needs scratch beyond the caller's inputs and outputs: the BF16
 // projection rows C = A . B^T and the per-block arrival counters, which the Python engine allocates through torch.
 // Some callers of this library have no device allocator they may use: a host process that binds the C-ABI from
-// another language and owns only the buffers it was handed, or code that runs while its stream is being captured,
-// where cudaMalloc is not allowed. morj_gemm_norm_epilogue_noalloc runs the same two kernels for one rank with that
+// another language, owns only the buffers it was handed and may not call cudaMalloc itself (its memory is managed
+// elsewhere, or its budget is fixed at start-up). morj_gemm_norm_epilogue_noalloc runs the same two kernels for one rank with that
 // scratch in a fixed array compiled into the library (kScratchBytes, every GPU that loads the library holds it until
 // exit), so it calls no cudaMalloc, cudaFree or other allocating routine.
 //

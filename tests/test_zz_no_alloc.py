@@ -2,8 +2,8 @@
 varies (`morj_gemm_bf16_peer` + `morj_peer_reduce` for one rank, scratch allocated by torch).
 
 It exists for callers that may not allocate device memory themselves, such as a process driving this library
-through its C-ABI with only the buffers it owns, or code running while its stream is captured; its scratch is a
-fixed array inside the library. Two calls in a row check that the second call is not disturbed by what the first
+through its C-ABI with only the buffers it owns and no right to call cudaMalloc; its scratch is a fixed array
+inside the library. Two calls in a row check that the second call is not disturbed by what the first
 left in that shared array. Collected last, so a run that stops at its first failure has run every other test."""
 import ctypes
 

@@ -4,9 +4,9 @@
 // projection rows C = A . B^T and the per-block arrival counters, which the Python engine allocates through torch.
 // Some callers of this library have no device allocator they may use: a host process that binds the C-ABI from
 // another language, owns only the buffers it was handed and may not call cudaMalloc itself (its memory is managed
-// elsewhere, or its budget is fixed at start-up). morj_gemm_norm_epilogue_noalloc runs the same two kernels for one rank with that
-// scratch in a fixed array compiled into the library (kScratchBytes, every GPU that loads the library holds it until
-// exit), so it calls no cudaMalloc, cudaFree or other allocating routine.
+// elsewhere, or its budget is fixed at start-up). morj_gemm_norm_epilogue_noalloc runs the same two kernels for one
+// rank with that scratch in a fixed array compiled into the library (kScratchBytes, every GPU that loads the library
+// holds it until exit), so it calls no cudaMalloc, cudaFree or other allocating routine.
 //
 // The array is shared by every call on a device and keeps the last call's contents: each call clears the counters
 // it uses (cudaMemsetAsync on its stream) before the GEMM, and the projection rows are fully rewritten. Two calls

@@ -162,8 +162,9 @@ int morj_geglu(const void* gu, int n, int F, void* out, void* stream);
  * its blocks from every rank (NVLink loads from peer memory), sums them in rank order in FP32, rounds to BF16 (the
  * value an NCCL BF16 all-reduce gives for two ranks), applies the post-attention or post-MLP epilogue to its own
  * rows, and stores the new h rows (and, when asked, x rows) into every rank's buffers, counting rows on their
- * per-block counters. A wait kernel then holds the stream until every row block of h has arrived. Counters only grow: the caller passes cumulative targets (site = one O or down
- * reduction; after s sites every block's partial counter reaches s * world * 4 * H and its row counter s * 128),
+ * per-block counters. A wait kernel then holds the stream until every row block of h has arrived. Counters only
+ * grow: the caller passes cumulative targets (site = one O or down reduction; after s sites every block's partial
+ * counter reaches s * world * 4 * H and its row counter s * 128),
  * and blocks past a call's rows are padded by the reduce kernel so the targets hold for every block.
  * Every wait is bounded (2 s): on expiry the kernel records MORJ device code 0x104 / 0x105 and returns. */
 #define MORJ_MAX_RANKS 8
@@ -204,8 +205,8 @@ int morj_peer_reduce(const morj_peer_t* peer, int mode, int n, const void* w_a, 
 int morj_peer_wait(const morj_peer_t* peer, int n, unsigned long long row_target, void* stream);
 
 /* No counterpart in the reference. For callers that cannot allocate device memory (a process binding this C-ABI
- * from another language that owns only the buffers it passes in and may not call cudaMalloc itself): the one-rank row-parallel projection and norm epilogue, C = A . B^T
- * ([M, N] BF16, N = H) followed by morj_peer_reduce's epilogue on every row (mode 0: post-attention, w_a = post_attn,
+ * from another language that owns only the buffers it passes in and may not call cudaMalloc itself): the one-rank
+ * row-parallel projection and norm epilogue, C = A . B^T ([M, N] BF16, N = H) followed by morj_peer_reduce's epilogue on every row (mode 0: post-attention, w_a = post_attn,
  * w_b = pre_ff, h required; mode 1: post-MLP, w_a = post_ff, scalar, w_b = next input norm, has_next). x is updated
  * in place, h written. Its scratch (the C rows and the block counters) is a fixed array inside the library, 8 MiB
  * plus 16 KiB, held by every GPU that loads the library until exit: M * N * 2 must not exceed 8 MiB (and M must not

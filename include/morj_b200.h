@@ -206,13 +206,14 @@ int morj_peer_wait(const morj_peer_t* peer, int n, unsigned long long row_target
 
 /* No counterpart in the reference. For callers that cannot allocate device memory (a process binding this C-ABI
  * from another language that owns only the buffers it passes in and may not call cudaMalloc itself): the one-rank
- * row-parallel projection and norm epilogue, C = A . B^T ([M, N] BF16, N = H) followed by morj_peer_reduce's epilogue on every row (mode 0: post-attention, w_a = post_attn,
- * w_b = pre_ff, h required; mode 1: post-MLP, w_a = post_ff, scalar, w_b = next input norm, has_next). x is updated
- * in place, h written. Its scratch (the C rows and the block counters) is a fixed array inside the library, 8 MiB
- * plus 16 KiB, held by every GPU that loads the library until exit: M * N * 2 must not exceed 8 MiB (and M must not
- * exceed 131072), larger calls are rejected with MORJ_ERR_ARG. The first call on a device looks the array's
- * address up (cudaGetSymbolAddress); make that first call before any stream capture. Every call shares the array:
- * calls that overlap on the GPU race and must be ordered by the caller. Allocates nothing. */
+ * row-parallel projection and norm epilogue, C = A . B^T ([M, N] BF16, N = H) followed by morj_peer_reduce's
+ * epilogue on every row (mode 0: post-attention, w_a = post_attn, w_b = pre_ff, h required; mode 1: post-MLP, w_a =
+ * post_ff, scalar, w_b = next input norm, has_next). x is updated in place, h written. Its scratch (the C rows and
+ * the block counters) is a fixed array inside the library, 8 MiB plus 16 KiB, held by every GPU that loads the
+ * library until exit: M * N * 2 must not exceed 8 MiB (and M must not exceed 131072), larger calls are rejected
+ * with MORJ_ERR_ARG. The first call on a device looks the array's address up (cudaGetSymbolAddress); make that
+ * first call before any stream capture. Every call shares the array: calls that overlap on the GPU race and must be
+ * ordered by the caller. Allocates nothing. */
 int morj_gemm_norm_epilogue_noalloc(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                                     int mode, void* x, void* h, const void* w_a, const void* scalar, const void* w_b,
                                     float eps, int has_next, void* stream);

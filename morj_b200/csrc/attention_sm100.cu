@@ -69,6 +69,37 @@ MORJ_DEV int key_slot(const int* __restrict__ kv_indices, int kv_base, int t, in
   return page * page_size + t % page_size;
 }
 
+// Packed pairs of FP32 values (one 64-bit register): fma / add on both lanes in one instruction, and a three-input
+// maximum.
+MORJ_DEV uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+MORJ_DEV uint64_t f2_bits(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+MORJ_DEV void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+MORJ_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+MORJ_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+MORJ_DEV float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // warp-level wait: lane 0 polls the barrier, the warp follows its verdict
 MORJ_DEV bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   int ok = (threadIdx.x & 31) == 0 ? (int)mbar_wait(bar, parity, abort, kErrTimeoutAttention) : 0;
@@ -297,7 +328,9 @@ __global__ void __launch_bounds__(THREADS, 2)
       for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
       if (__all_sync(0xffffffffu, full)) {
 #pragma unroll
-        for (int j = 0; j < BN; ++j) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(sr[j >> 5][j & 31]));
+        for (int j = 0; j < BN; j += 2)
+          m8[(j >> 1) & 7] = max3f(m8[(j >> 1) & 7], __uint_as_float(sr[j >> 5][j & 31]),
+                                   __uint_as_float(sr[(j + 1) >> 5][(j + 1) & 31]));
       } else {
 #pragma unroll
         for (int j = 0; j < BN; ++j) {
@@ -307,7 +340,8 @@ __global__ void __launch_bounds__(THREADS, 2)
           m8[j & 7] = fmaxf(m8[j & 7], v);
         }
       }
-      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= scale_log2;  // scale > 0: the maximum of the scaled scores
       float alpha = 1.f;
       if (mx > m_used + RESCALE_LOG2 || m_used == -INFINITY) {
@@ -317,18 +351,28 @@ __global__ void __launch_bounds__(THREADS, 2)
       l_run *= alpha;
       // exp2(-inf) = 0 for masked keys; a row with no visible key yet keeps m_used = -inf and p = 0
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-      float s8[8];
+      // scores in pairs: one packed FMA scales and shifts two of them, one packed add sums two probabilities
+      const uint64_t scale2 = f2_pack(scale_log2, scale_log2), neg_m2 = f2_pack(neg_m, neg_m);
+      uint64_t s4[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
+      for (int i = 0; i < 4; ++i) s4[i] = f2_pack(0.f, 0.f);
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int j = 0; j < BN; j += 2) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[j >> 5][j & 31]), scale_log2, neg_m));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[(j + 1) >> 5][(j + 1) & 31]), scale_log2, neg_m));
-        s8[(j >> 1) & 7] += p0 + p1;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_bits(sr[j >> 5][j & 31], sr[(j + 1) >> 5][(j + 1) & 31]), scale2, neg_m2), x0, x1);
+        const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+        s4[(j >> 1) & 3] = f2_add(s4[(j >> 1) & 3], f2_pack(p0, p1));
         pk[j / 2] = pack_bf16x2(p0, p1);
       }
-      l_run += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo, hi;
+        f2_unpack(s4[i], lo, hi);
+        sum += lo + hi;
+      }
+      l_run += sum;
       // a rescale of O waits until the previous chunk's PV has completed (the next one needs this chunk's P)
       if (c >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
         if (!warp_wait(pv_done + 8 * (b ^ 1), ((c - 1) >> 1) & 1, abort)) {

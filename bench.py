@@ -286,6 +286,9 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--workload', default='text', choices=['text', 'multimodal', 'latency', 'sweep'])
+    ap.add_argument('--layers', type=int, default=0,
+                    help='profiling only: the 31B-class model cut to its first L layers (same row and GEMM shapes, '
+                         'a few GB on the device); 0 = all 60')
     ap.add_argument('--tp-comm', default='peer', choices=['peer', 'nccl'],
                     help='tensor parallelism: reduce over peer memory fused with the epilogues, or NCCL all-reduce')
     ap.add_argument('--mode', default='replicas', choices=['replicas', 'tp'],
@@ -332,6 +335,8 @@ def main():
 
     tp = args.mode == 'tp' and world > 1
     top = w.gemma31b_config()
+    if args.layers:
+        top = w.reduced_config(top, args.layers)
     t_init = time.perf_counter()
     model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD if tp else None,
                                    tp_comm=args.tp_comm)
@@ -461,7 +466,9 @@ def main():
             ms_per_step=ms_max, higher_is_better=True, scaling='strong' if tp else 'weak', vs_baseline=None,
             dtype='bf16',
             data='synthetic (seeded random-init weights N(0, 0.02), uniform token ids)',
-            config=dict(workload=f'31B-class Gemma-style decoder, {desc}', tokens=tokens,
+            config=dict(workload=(f'31B-class Gemma-style decoder, {desc}' if not args.layers else
+                                  f'31B-class Gemma-style decoder cut to {args.layers} layers (profiling), {desc}'),
+                        tokens=tokens,
                         parallelism=((f'tensor parallel x{world} (O/down partial rows read by their row owners '
                                       f'over NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else
                                       f'tensor parallel x{world} (NCCL all-reduce after O and down)') if tp else

@@ -205,6 +205,10 @@ def kernel_arm(args):
     sys.path.insert(0, os.path.join(ROOT, 'tests'))
     dev = torch.device('cuda', 0)
     s = torch.cuda.current_stream().cuda_stream
+    ws = None
+    if not args.no_split:  # (the engine's configuration: split tiles on its stream)
+        ws = nat.GemmWorkspace(dev)
+        ws.register(s)
     if args.kernel == 'qkv':
         # the sliding-layer QKV projection with the fused head norm + RoPE + pool scatter epilogue
         M, H, d, hq, hk = args.m, 5376, 128, 32, 16
@@ -277,6 +281,8 @@ def kernel_arm(args):
                           frac_of_burst_peak=round(tf / pk['bf16'], 4), peak_source=pk['source'],
                           gflop=round(flops / 1e9, 2))), flush=True)
     assert nat.device_error(s) == 0
+    if ws is not None:
+        ws.close()
 
 
 def main():
@@ -297,6 +303,8 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window'],
                     help='time one kernel alone instead of the tree forward')
+    ap.add_argument('--no-split', action='store_true',
+                    help='no split-tile workspace registered (every GEMM tile computed whole)')
     ap.add_argument('--force', type=lambda v: int(v, 0), default=0,
                     help='kernel mode: or-ed into the GEMM epilogue (0x100 SM-pair kernel, 0x200 one-CTA kernel)')
     ap.add_argument('--m', type=int, default=2040)
@@ -340,6 +348,9 @@ def main():
     t_init = time.perf_counter()
     model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD if tp else None,
                                    tp_comm=args.tp_comm)
+    if args.no_split and model.gemm_ws is not None:  # every GEMM tile computed whole
+        model.gemm_ws.close()
+        model.gemm_ws = None
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t_init
     tree_in, desc = workload(args.workload, 0 if tp else rank)

@@ -71,6 +71,26 @@ int morj_device_error(int* code, int clear, void* stream);
 int morj_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
                    int K, int epilogue, void* stream);
 
+/* Split-tile workspace of the SM-pair GEMM kernel (an addition; the reference's cuBLAS calls have no counterpart).
+ * With a workspace registered for a stream, the pair-kernel GEMMs launched on that stream (morj_gemm_bf16,
+ * morj_gemm_qkv_rope, morj_gemm_bf16_peer and morj_gemm_norm_epilogue_noalloc) share the k-blocks of the tiles that
+ * do not fill a whole wave of SM pairs evenly between all pairs: a tile cut between two pairs sends the FP32 partial
+ * of its first k-blocks through the workspace. Without one, every tile is computed whole (same results up to FP32
+ * summation order). The memory is the caller's: at least morj_gemm_workspace_bytes() bytes (about 19 MB on a
+ * 148-SM B200), 256-byte aligned, used by one stream only (launches on one stream run in order; two streams must
+ * not share a workspace). morj_gemm_workspace_set zeroes the workspace's flags on `stream` and replaces any earlier
+ * registration for (current device, stream); ptr = NULL removes it. morj_gemm_workspace_remove drops every
+ * registration of `ptr` (call it before freeing the memory). At most 64 registrations. */
+int morj_gemm_workspace_bytes(unsigned long long* bytes);
+int morj_gemm_workspace_set(void* stream, void* ptr, unsigned long long bytes);
+int morj_gemm_workspace_remove(const void* ptr);
+
+/* The split schedule (host function, no device access): the work items pair `pair` of `pairs` walks for a GEMM of
+ * `tiles` tiles of `kblocks` k-blocks, in order, as (tile, first k-block, end k-block, kind) int quadruples, kind
+ * 0 = whole tile, 1 = first k-blocks of a cut tile (partial to the workspace), 2 = last k-blocks (adds the partial,
+ * then the epilogue). Returns the number of items, -1 on bad arguments or when cap is too small. */
+int morj_gemm_split_walk(int tiles, int pairs, int kblocks, int pair, int* items, int cap);
+
 /* The QKV projection with the head epilogue fused: [q | k | v] = A . W^T (W: [N, K] rows q heads, k heads, v heads if
  * has_v; N = (hq + (1 + has_v) * hk) * d), each head RMSNorm'ed over the BF16-rounded projection (q, k weighted;
  * v unweighted), rounded, RoPE'd (q, k) and written straight to q_out[row, hq, d] and pool row slots[row] of

@@ -28,6 +28,10 @@ SIGNATURES = {
     'morj_version': [],
     'morj_device_error': [IP, I, P],
     'morj_gemm_bf16': [P, LL, P, LL, P, LL, I, I, I, I, P],
+    'morj_gemm_workspace_bytes': [ctypes.POINTER(ctypes.c_ulonglong)],
+    'morj_gemm_workspace_set': [P, P, ctypes.c_ulonglong],
+    'morj_gemm_workspace_remove': [P],
+    'morj_gemm_split_walk': [I, I, I, I, IP, I],
     'morj_gemm_qkv_rope': [P, LL, P, LL, I, I, I, I, I, I, P, P, P, P, I, P, F, P, P, P, P],
     'morj_rope_table': [P, I, I, P, P],
     'morj_embed_rmsnorm': [P, P, P, P, I, I, F, P, F, P, P, P],
@@ -133,3 +137,51 @@ def device_error(stream, clear=True):
     code = ctypes.c_int(0)
     check(lib().morj_device_error(ctypes.byref(code), int(clear), stream), 'morj_device_error')
     return code.value
+
+
+def gemm_workspace_bytes():
+    """Bytes of a split-tile workspace for the pair GEMM kernel on the current device."""
+    n = ctypes.c_ulonglong(0)
+    check(lib().morj_gemm_workspace_bytes(ctypes.byref(n)), 'morj_gemm_workspace_bytes')
+    return n.value
+
+
+def split_walk(tiles, pairs, kblocks, pair):
+    """The pair GEMM kernel's work items for SM pair `pair`, in order: an [n, 4] int32 array of
+    (tile, first k-block, end k-block, kind) with kind 0 whole, 1 head of a cut tile, 2 tail of a cut tile."""
+    import numpy as np
+    cap = tiles // max(1, pairs) + 4
+    buf = np.zeros(4 * cap, dtype=np.int32)
+    n = lib().morj_gemm_split_walk(tiles, pairs, kblocks, pair, buf.ctypes.data_as(IP), cap)
+    if n < 0:
+        check(ERR_ARG, 'morj_gemm_split_walk')
+    return buf[:4 * n].reshape(n, 4)
+
+
+class GemmWorkspace:
+    """Device memory for the pair GEMM kernel's split tiles, registered (`morj_gemm_workspace_set`) for each stream it
+    serves; `close()` (or garbage collection) unregisters it before the memory goes back to torch."""
+
+    def __init__(self, device):
+        import torch
+        self.nbytes = gemm_workspace_bytes()
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.ptr = self.buf.data_ptr()
+        self.streams = set()
+
+    def register(self, stream):
+        if self.ptr and stream not in self.streams:
+            call('morj_gemm_workspace_set', stream, self.ptr, self.nbytes)
+            self.streams.add(stream)
+
+    def close(self):
+        if self.ptr:
+            lib().morj_gemm_workspace_remove(self.ptr)
+            self.ptr = None
+            self.streams.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

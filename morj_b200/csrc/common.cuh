@@ -28,6 +28,7 @@ enum DeviceError : int {
   kErrTimeoutGemmEpilogue = 0x103,
   kErrTimeoutPeerPartials = 0x104,
   kErrTimeoutPeerRows = 0x105,
+  kErrTimeoutGemmSplit = 0x106,
   kErrTimeoutAttention = 0x201,
   kErrBadIndex = 0x301,
   kErrBadAlignment = 0x302,

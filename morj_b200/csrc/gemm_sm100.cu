@@ -6,7 +6,8 @@
 //               stage back to the producer and each finished tile to the epilogue
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (thread = row), BF16 rounding and the fused epilogue
 // Two accumulators (all 512 TMEM columns) let the epilogue of tile i overlap the main loop of i+1. The tile width
-// BN (128..256) is chosen per shape so the tile count fills whole waves of the 148 SMs.
+// BN (128..256) is chosen per shape so the tile count fills whole waves of the 148 SMs; with a caller-registered
+// workspace the SM-pair kernel instead shares the k-blocks of its last waves evenly between the pairs (split tiles).
 // Tiles are walked in groups of 16 row-blocks so the activation slice and the weight tiles of the CTAs in flight
 // stay in L2. No TMA multicast is used, so the kernel is valid whichever GPU's memory the pointers refer to.
 #include <mutex>
@@ -62,6 +63,140 @@ struct PeerEpi {
   unsigned long long* partials[MORJ_MAX_RANKS];
   int world;
 };
+
+// Split tiles of the pair kernel. When the tiles do not fill whole waves of SM pairs, the tiles of the last one to
+// two waves are cut along K so that every pair gets the same number of k-blocks. Tiles [0, dp_tiles) go whole to
+// pair t % pairs. The k-blocks of tiles [dp_tiles, tiles), `units` of them in tile-major order, are cut into `pairs`
+// contiguous ranges of equal length (to one k-block), range p going to pair p. The host splits between `pairs` and
+// 2 * pairs - 1 tiles this way, so a range is at least one tile long and a tile is cut at most once: its k-head
+// [0, b) ends range p and its k-tail [b, kb) starts range p + 1. A pair walks its range from the end: the head
+// piece first (kHead: its FP32 partial goes to the pair's workspace slot), then its whole tiles, the tail piece last
+// (kTail: adds the slot of pair p - 1, written at that pair's start, then runs the epilogue). A pair thus only waits
+// on a lower pair, for a partial written early in that pair's share of the split tiles.
+struct Split {
+  float4* ws;       // partial tiles: [pair][rank][epilogue warp][kSlotChunks float4 columns][32 rows]
+  unsigned* flags;  // [pair][rank][epilogue warp]: 1 while the slot holds a partial not yet added
+  int dp_tiles;
+  long long units;
+};
+constexpr int kSlotChunks = 256 / 4;                                  // float4 columns of a 256-wide partial row
+constexpr size_t kSlotBytesPerPair = 2ull * 4 * kSlotChunks * 32 * 16;  // both CTAs, 4 warps of 32 rows each
+constexpr size_t kFlagBytesPerPair = 2 * 4 * sizeof(unsigned);
+
+enum : int { kWhole = 0, kHead = 1, kTail = 2 };
+struct Item {
+  int tile, k0, k1, kind;  // k-blocks [k0, k1) of `tile`
+};
+struct Walk {
+  int pairs, kb, dp_tiles, t;
+  long long lo, hi;  // what is left of this pair's range of split k-blocks, taken from the end
+  __host__ __device__ Walk(int pair, int pairs_, int kb_, int dp, long long units)
+      : pairs(pairs_), kb(kb_), dp_tiles(dp), t(pair), lo(units * pair / pairs_), hi(units * (pair + 1) / pairs_) {}
+  __host__ __device__ bool next(Item& it) {
+    if (t < dp_tiles) {
+      it = Item{t, 0, kb, kWhole};
+      t += pairs;
+      return true;
+    }
+    if (hi <= lo) return false;
+    const long long first = (hi - 1) / kb * kb;  // first k-block of the tile that holds k-block hi - 1
+    const long long s = first > lo ? first : lo;
+    it.tile = dp_tiles + (int)((hi - 1) / kb);
+    it.k0 = (int)(s - first);
+    it.k1 = (int)(hi - first);
+    it.kind = it.k0 > 0 ? kTail : (it.k1 < kb ? kHead : kWhole);
+    hi = s;
+    return true;
+  }
+};
+
+// The split of `tiles` tiles of `kb` k-blocks over `pairs` SM pairs (no split: dp_tiles = tiles, units = 0).
+__host__ __device__ inline void split_schedule(int tiles, int pairs, int kb, int* dp_tiles, long long* units) {
+  *dp_tiles = tiles;
+  *units = 0;
+  if (pairs < 2 || tiles <= pairs || tiles % pairs == 0) return;
+  *dp_tiles = (tiles / pairs - 1) * pairs;
+  *units = (long long)(tiles - *dp_tiles) * kb;
+}
+
+MORJ_DEV unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+MORJ_DEV void st_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+MORJ_DEV void st_relaxed_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// kHead: this warp's 32 accumulator rows (FP32) to its slot, column-chunk-major so each store is one 512-byte line
+// per warp; then the flag, released after every lane's stores.
+template <int BN>
+MORJ_DEV void save_partial(uint32_t tacc, float4* slot, unsigned* flag, int lane) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(tacc + c, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      __stcg(slot + (c / 4 + v) * 32 + lane, make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                         __uint_as_float(r[4 * v + 2]),
+                                                         __uint_as_float(r[4 * v + 3])));
+  }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_gpu(flag, 1u);
+}
+
+// kTail: wait (bounded) for the head's partial, add it into this warp's accumulator rows in TMEM and clear the flag
+// for the next launch. Returns false when the wait gave up (device error recorded, CTA abort raised).
+template <int BN>
+MORJ_DEV bool add_partial(uint32_t tacc, const float4* slot, unsigned* flag, int lane, volatile int* abort) {
+  int ok = 1;
+  if (lane == 0) {
+    const unsigned long long t0 = global_ns();
+    for (uint32_t i = 0; ld_acquire_gpu(flag) == 0; ++i) {
+      if ((i & 63) == 63) {
+        if (*abort) {
+          ok = 0;
+          break;
+        }
+        if (global_ns() - t0 > kWaitLimitNs) {
+          *abort = 1;
+          report(kErrTimeoutGemmSplit);
+          ok = 0;
+          break;
+        }
+      }
+      __nanosleep(128);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return false;
+  (void)ld_acquire_gpu(flag);  // (every lane acquires the head's stores)
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(tacc + c, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const float4 p = __ldcg(slot + (c / 4 + v) * 32 + lane);
+      r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + p.x);
+      r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + p.y);
+      r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + p.z);
+      r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + p.w);
+    }
+    tmem_st32(tacc + c, r);
+  }
+  tmem_wait_st();
+  __syncwarp();
+  if (lane == 0) st_relaxed_gpu(flag, 0u);
+  return true;
+}
 
 // (after a system fence by every lane and a warp barrier, which order the warp's stores before it)
 MORJ_DEV void red_relaxed_sys_add(unsigned long long* p, unsigned long long v) {
@@ -468,7 +603,7 @@ template <int EPI, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                  __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const QkvEpi qe,
-                 const PeerEpi pe) {
+                 const PeerEpi pe, const Split sp) {
   using C_ = Cfg2<BN>;
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
@@ -522,10 +657,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const uint64_t pol_b = policy_evict_normal();
       int stage = 0, issued = 0;
       uint32_t phase = 0;
-      for (int t = cluster; t < tiles && !*abort; t += n_clusters) {
-        const TileCoord tc = tile_coord(t, num_m, num_n);
+      Walk walk(cluster, n_clusters, kblocks, sp.dp_tiles, sp.units);
+      Item it;
+      while (!*abort && walk.next(it)) {
+        const TileCoord tc = tile_coord(it.tile, num_m, num_n);
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = it.k0; kb < it.k1; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kErrTimeoutGemmProducer)) {
             ok = false;
             break;
@@ -559,12 +696,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = cluster; t < tiles; t += n_clusters) {
+      Walk walk(cluster, n_clusters, kblocks, sp.dp_tiles, sp.units);
+      Item it;
+      while (walk.next(it)) {
         if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kErrTimeoutGemmMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * 256;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = it.k0; kb < it.k1; ++kb) {
           if (!mbar_wait(full0 + 8 * stage, phase, abort, kErrTimeoutGemmMma)) {
             ok = false;
             break;
@@ -574,7 +713,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_bf16_pair(d_tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), C_::IDESC, (kb | k) != 0);
+            umma_bf16_pair(d_tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), C_::IDESC,
+                           ((kb - it.k0) | k) != 0);
           }
           umma_commit_pair(empty0 + 8 * stage);
           if (++stage == STAGES) {
@@ -600,8 +740,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     unsigned long long* pend = nullptr;  // partial-delivery epilogue: the arrival still to post
     unsigned long long pend_cols = 0;
-    for (int t = cluster; t < tiles; t += n_clusters) {
-      const TileCoord tc = tile_coord(t, num_m, num_n);
+    Walk walk(cluster, n_clusters, kblocks, sp.dp_tiles, sp.units);
+    Item it;
+    while (walk.next(it)) {
+      const TileCoord tc = tile_coord(it.tile, num_m, num_n);
       int ok = lane == 0 ? (int)mbar_wait(accf0 + 8 * acc, acc_phase, abort, kErrTimeoutGemmEpilogue) : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if constexpr (EPI == EPI_PEER) peer_arrive(pend, pend_cols, lane);
@@ -609,7 +751,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int row = tc.m * 2 * BM + rank * BM + quarter * 32 + lane;
       const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
-      if constexpr (EPI == MORJ_EPI_QKV_D128) {
+      const int slot = (cluster * 2 + (int)rank) * 4 + quarter;  // this warp's slot (and flag) in pair `cluster`
+      if (it.kind == kHead) {
+        save_partial<BN>(tacc, sp.ws + (size_t)slot * kSlotChunks * 32, sp.flags + slot, lane);
+      } else if (it.kind == kTail && !add_partial<BN>(tacc, sp.ws + (size_t)(slot - 8) * kSlotChunks * 32,
+                                                       sp.flags + slot - 8, lane, abort)) {
+        break;
+      } else if constexpr (EPI == MORJ_EPI_QKV_D128) {
         epilogue_qkv<BN, 128>(tacc, row, tc.n, row < M, qe, N);
       } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
         epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
@@ -721,6 +869,33 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
   return check_launch("gemm_kernel");
 }
 
+// Split-tile workspaces, one per (device, stream), registered by the caller (morj_gemm_workspace_set): the pair
+// kernel's FP32 partial tiles and their flags live in memory the caller owns, so no launch allocates and launches on
+// different streams never share one.
+struct Workspace {
+  int dev;
+  cudaStream_t stream;
+  void* ptr;
+};
+constexpr int kMaxWorkspaces = 64;
+static Workspace g_ws[kMaxWorkspaces];
+static int g_ws_count = 0;
+static std::mutex g_ws_lock;
+
+static unsigned long long workspace_bytes() {
+  return (unsigned long long)(num_sms() / 2) * (kSlotBytesPerPair + kFlagBytesPerPair);
+}
+
+// The workspace registered for `stream` on the current device, or nullptr.
+static void* workspace_for(cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> g(g_ws_lock);
+  for (int i = 0; i < g_ws_count; ++i)
+    if (g_ws[i].dev == dev && g_ws[i].stream == stream) return g_ws[i].ptr;
+  return nullptr;
+}
+
 template <int EPI, int BN>
 static int launch2(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
                    int K, cudaStream_t stream, const QkvEpi& qe = QkvEpi{}, const PeerEpi& pe = PeerEpi{}) {
@@ -740,21 +915,30 @@ static int launch2(const void* A, long long lda, const void* B, long long ldb, v
   const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
   const int pairs = num_sms() / 2;
   const int clusters = tiles < pairs ? tiles : pairs;
+  Split sp{nullptr, nullptr, tiles, 0};
+  if (void* ws = workspace_for(stream)) {
+    split_schedule(tiles, pairs, (K + BK - 1) / BK, &sp.dp_tiles, &sp.units);
+    if (sp.units) {  // (only when tiles > pairs: every pair of the grid takes part)
+      sp.ws = static_cast<float4*>(ws);
+      sp.flags = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)pairs * kSlotBytesPerPair);
+    }
+  }
   gemm2_kernel<EPI, BN><<<2 * clusters, THREADS, C_::SMEM_BYTES, stream>>>(
-      ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe);
+      ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe, sp);
   return check_launch("gemm2_kernel");
 }
 
 // Kernel and tile width: the smallest (waves x per-tile time) over the candidates. A wave is one tile per SM (one
 // 256-row tile per SM pair for the pair kernel); a tile's time per 64-deep k-block is the larger of its MMA time
 // (2 x BN cycles) and the time to fill its stage from L2 (about 1.46 cycles per 128-byte row, measured on the 31B
-// shapes: 128 + BN rows for one CTA, 128 + BN / 2 per SM for the pair). Ties go to the pair kernel, then to the wider
-// tile.
+// shapes: 128 + BN rows for one CTA, 128 + BN / 2 per SM for the pair). With split tiles (`split`: a workspace is
+// registered for the stream) the pair kernel's last waves are shared out evenly, so its wave count is fractional
+// once there are more tiles than pairs. Ties go to the pair kernel, then to the wider tile.
 struct Choice {
   int bn;
   bool pair;
 };
-static Choice pick(int M, int N, const int* cand, int n_cand, int force) {
+static Choice pick(int M, int N, const int* cand, int n_cand, int force, bool split = false) {
   const int sms = num_sms();
   Choice best{cand[0], false};
   double best_cost = -1;
@@ -767,7 +951,8 @@ static Choice pick(int M, int N, const int* cand, int n_cand, int force) {
       const int slots = p ? sms / 2 : sms;
       const double fill = 1.46 * (BM + (p ? bn / 2 : bn));
       const double per_tile = 2.0 * bn > fill ? 2.0 * bn : fill;
-      const double cost = (double)((tiles + slots - 1) / slots) * per_tile;
+      const double waves = (p && split && tiles > slots) ? (double)tiles / slots : (double)((tiles + slots - 1) / slots);
+      const double cost = waves * per_tile;
       if (best_cost < 0 || cost < best_cost - 1e-9) {
         best_cost = cost;
         best = Choice{bn, p == 1};
@@ -796,7 +981,7 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
   if (epilogue == MORJ_EPI_STORE) {
     if (N % 16 || ldc < N) return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: N must be a multiple of 16 (N=%d)", N);
     static const int cand[] = {256, 240, 224, 208, 192, 176, 160, 128};
-    const gemm::Choice c = gemm::pick(M, N, cand, 8, force);
+    const gemm::Choice c = gemm::pick(M, N, cand, 8, force, gemm::workspace_for(s) != nullptr);
 #define MORJ_STORE_CASE(W)                                                                   \
   case W:                                                                                    \
     return c.pair ? gemm::launch2<MORJ_EPI_STORE, W>(A, lda, B, ldb, C, ldc, M, N, K, s)     \
@@ -819,7 +1004,7 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
     if (N % 256 || ldc < N / 2)
       return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: GEGLU needs N a multiple of 256 (N=%d)", N);
     static const int cand[] = {256};
-    if (gemm::pick(M, N, cand, 1, force).pair)
+    if (gemm::pick(M, N, cand, 1, force, gemm::workspace_for(s) != nullptr).pair)
       return gemm::launch2<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
     return gemm::launch<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
   }
@@ -851,7 +1036,8 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
   pe.world = peer->world;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   static const int cand[] = {256, 208, 192, 128};
-  const gemm::Choice c = gemm::pick(M, N, cand, 4, 0);  // (the widths the STORE path picks for these shapes)
+  // (the widths the STORE path picks for these shapes)
+  const gemm::Choice c = gemm::pick(M, N, cand, 4, 0, gemm::workspace_for(s) != nullptr);
   const gemm::QkvEpi qe{};
 #define MORJ_PEER_CASE(W)                                                                                        \
   case W:                                                                                                        \
@@ -891,10 +1077,12 @@ extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, l
                  (const float4*)rope, rope_rows, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool,
                  (__nv_bfloat16*)v_pool};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // One-CTA kernel unless forced: with the head epilogue (RMSNorm + sincos RoPE per element, one epilogue warp per
-  // scheduler) the pair kernel measured slower (2040 x 8192 x 5376: 0.192 ms pair, 0.158 ms one-CTA).
+  // Without split tiles the one-CTA kernel unless forced: the pair kernel's whole waves then favour 128-wide tiles,
+  // which pay the head epilogue twice as often (2040 x 8192 x 5376: 0.20 ms pair at BN 128, 0.158 ms one-CTA). With a
+  // workspace, the choice per shape (2040 x 8192 x 5376: the pair kernel at BN 256).
   static const int cand[] = {256, 128};
-  const gemm::Choice c = gemm::pick(M, N, cand, 2, force ? force : 2);
+  const bool split = gemm::workspace_for(s) != nullptr;
+  const gemm::Choice c = gemm::pick(M, N, cand, 2, force ? force : (split ? 0 : 2), split);
   if (d == 128) {
     if (c.bn == 128)
       return c.pair ? gemm::launch2<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)
@@ -910,4 +1098,76 @@ extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, l
                   : gemm::launch<MORJ_EPI_QKV_D64, 256>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e);
   }
   return set_error(MORJ_ERR_UNSUPPORTED, "morj_gemm_qkv_rope: head_dim %d unsupported (64, 128)", d);
+}
+
+extern "C" int morj_gemm_workspace_bytes(unsigned long long* bytes) {
+  if (!bytes) return morj::set_error(MORJ_ERR_ARG, "morj_gemm_workspace_bytes: null output");
+  *bytes = morj::gemm::workspace_bytes();
+  return MORJ_OK;
+}
+
+extern "C" int morj_gemm_workspace_set(void* stream, void* ptr, unsigned long long bytes) {
+  using namespace morj;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (ptr) {
+    const unsigned long long need = gemm::workspace_bytes();
+    if (reinterpret_cast<uintptr_t>(ptr) & 255)
+      return set_error(MORJ_ERR_ARG, "morj_gemm_workspace_set: the workspace must be 256-byte aligned");
+    if (bytes < need)
+      return set_error(MORJ_ERR_ARG, "morj_gemm_workspace_set: %llu bytes given, %llu needed", bytes, need);
+    const size_t pairs = num_sms() / 2;
+    e = cudaMemsetAsync(static_cast<char*>(ptr) + pairs * gemm::kSlotBytesPerPair, 0,
+                        pairs * gemm::kFlagBytesPerPair, s);
+    if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  }
+  std::lock_guard<std::mutex> g(gemm::g_ws_lock);
+  for (int i = 0; i < gemm::g_ws_count; ++i) {
+    if (gemm::g_ws[i].dev == dev && gemm::g_ws[i].stream == s) {
+      if (ptr)
+        gemm::g_ws[i].ptr = ptr;
+      else
+        gemm::g_ws[i] = gemm::g_ws[--gemm::g_ws_count];
+      return MORJ_OK;
+    }
+  }
+  if (!ptr) return MORJ_OK;
+  if (gemm::g_ws_count == gemm::kMaxWorkspaces)
+    return set_error(MORJ_ERR_UNSUPPORTED, "morj_gemm_workspace_set: more than %d streams", gemm::kMaxWorkspaces);
+  gemm::g_ws[gemm::g_ws_count++] = gemm::Workspace{dev, s, ptr};
+  return MORJ_OK;
+}
+
+extern "C" int morj_gemm_workspace_remove(const void* ptr) {
+  using namespace morj;
+  std::lock_guard<std::mutex> g(gemm::g_ws_lock);
+  for (int i = 0; i < gemm::g_ws_count;) {
+    if (gemm::g_ws[i].ptr == ptr)
+      gemm::g_ws[i] = gemm::g_ws[--gemm::g_ws_count];
+    else
+      ++i;
+  }
+  return MORJ_OK;
+}
+
+extern "C" int morj_gemm_split_walk(int tiles, int pairs, int kblocks, int pair, int* items, int cap) {
+  using namespace morj::gemm;
+  if (tiles < 0 || pairs < 1 || kblocks < 1 || pair < 0 || pair >= pairs || cap < 0 || (cap && !items)) return -1;
+  int dp = 0;
+  long long units = 0;
+  split_schedule(tiles, pairs, kblocks, &dp, &units);
+  Walk walk(pair, pairs, kblocks, dp, units);
+  Item it;
+  int n = 0;
+  while (walk.next(it)) {
+    if (n == cap) return -1;
+    items[4 * n] = it.tile;
+    items[4 * n + 1] = it.k0;
+    items[4 * n + 2] = it.k1;
+    items[4 * n + 3] = it.kind;
+    ++n;
+  }
+  return n;
 }

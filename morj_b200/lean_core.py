@@ -248,6 +248,8 @@ class LeanGemma4:
         self.h2d_bytes = 0
         self.launches = 0
         self.trace = None
+        # split-tile workspace of the pair GEMM kernel, registered for every stream the model launches on
+        self.gemm_ws = nat.GemmWorkspace(self.device) if self.device.type == 'cuda' else None
         if tp_group is not None and tp_comm == 'peer':
             from .tp import PeerExchange
             self.peer = PeerExchange(tp_group, self.hidden, max(single_max, step_tokens), self.device)
@@ -344,7 +346,10 @@ class LeanGemma4:
         return pools
 
     def _stream(self):
-        return torch.cuda.current_stream(self.device).cuda_stream
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        if self.gemm_ws is not None:
+            self.gemm_ws.register(s)
+        return s
 
     # ---- pass -----------------------------------------------------------------------------------------------------
     def plan(self, req, seqs, available=None):

@@ -1077,12 +1077,13 @@ extern "C" int morj_gemm_qkv_rope(const void* A, long long lda, const void* W, l
                  (const float4*)rope, rope_rows, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool,
                  (__nv_bfloat16*)v_pool};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // Without split tiles the one-CTA kernel unless forced: the pair kernel's whole waves then favour 128-wide tiles,
-  // which pay the head epilogue twice as often (2040 x 8192 x 5376: 0.20 ms pair at BN 128, 0.158 ms one-CTA). With a
-  // workspace, the choice per shape (2040 x 8192 x 5376: the pair kernel at BN 256).
+  // The head epilogue costs about as much per 128 columns as 35 k-blocks of main loop, which the cost model does not
+  // see: 128-wide tiles pay it twice as often. So without split tiles (or with at most one 256-row block) the
+  // one-CTA kernel unless forced (2040 x 8192 x 5376: 0.20 ms pair at BN 128, 0.158 ms one-CTA); with them, BN 256
+  // and the kernel per shape (2040 x 8192 x 5376: the pair kernel, 0.146 ms).
   static const int cand[] = {256, 128};
-  const bool split = gemm::workspace_for(s) != nullptr;
-  const gemm::Choice c = gemm::pick(M, N, cand, 2, force ? force : (split ? 0 : 2), split);
+  const bool split = gemm::workspace_for(s) != nullptr && M > 2 * gemm::BM;
+  const gemm::Choice c = gemm::pick(M, N, cand, split ? 1 : 2, force ? force : (split ? 0 : 2), split);
   if (d == 128) {
     if (c.bn == 128)
       return c.pair ? gemm::launch2<MORJ_EPI_QKV_D128, 128>(A, lda, W, ldw, nullptr, 0, M, N, K, s, e)

@@ -154,6 +154,8 @@ __global__ void __launch_bounds__(THREADS, 2)
                           const int* __restrict__ qo_indptr, const int* __restrict__ kv_indptr,
                           const int* __restrict__ kv_indices, const int* __restrict__ kv_last_page_len, int n_bidir,
                           int hq, int hk, int page_size, int window, float scale_log2, const int* __restrict__ work) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   using L = Smem<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -461,11 +463,11 @@ static int launch(const void* q, int n_q, const void* k_pool, const void* v_pool
     if (st) return st;
   }
   dim3 grid(n_work, hk);
-  tree_attention_kernel<D><<<grid, THREADS, Smem<D>::TOTAL, stream>>>(
-      qm, km, vm, reinterpret_cast<const __nv_bfloat16*>(k_pool), reinterpret_cast<const __nv_bfloat16*>(v_pool),
-      reinterpret_cast<__nv_bfloat16*>(out), qo_indptr, kv_indptr, kv_indices, kv_last_page_len, n_bidir, hq, hk,
-      page_size, window, sm_scale * LOG2E, work);
-  return check_launch("tree_attention_kernel");
+  return launch_pdl("tree_attention_kernel", tree_attention_kernel<D>, grid, dim3(THREADS), Smem<D>::TOTAL, stream,
+                    qm, km, vm, reinterpret_cast<const __nv_bfloat16*>(k_pool),
+                    reinterpret_cast<const __nv_bfloat16*>(v_pool), reinterpret_cast<__nv_bfloat16*>(out), qo_indptr,
+                    kv_indptr, kv_indices, kv_last_page_len, n_bidir, hq, hk, page_size, window, sm_scale * LOG2E,
+                    work);
 }
 
 }  // namespace attn

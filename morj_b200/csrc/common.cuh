@@ -387,6 +387,34 @@ MORJ_DEV float gelu_tanh(float x) {
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 
+// ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of this library is launched with launch_pdl, so the GPU may schedule
+// it (and it may run its prologue: barrier set-up, TMEM allocation, tensor-map prefetch) while the previous kernel on
+// the stream is still finishing. pdl_wait() returns once that kernel has completed and its memory operations are
+// visible: each kernel calls it before its first access to global memory. pdl_trigger() lets the next kernel's CTAs
+// be scheduled; it orders nothing, the next kernel's own pdl_wait() does.
+// ---------------------------------------------------------------------------------------------------------------
+MORJ_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MORJ_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t stream, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return MORJ_OK;
+}
+
 // host side: tiled tensor maps (driver entry point resolved at run time; gemm_sm100.cu)
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* ptr, const unsigned long long* dims,
                  const unsigned long long* strides_bytes, const unsigned* box, CUtensorMapSwizzle swizzle);

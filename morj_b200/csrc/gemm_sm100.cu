@@ -458,6 +458,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // (set-up above touches no global memory) the previous kernel on the stream has completed
+  pdl_trigger();
 
   const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n;
@@ -642,6 +644,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   cluster_sync();  // barriers of both CTAs are initialised before either CTA signals the other's
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // (set-up above touches no global memory) the previous kernel on the stream has completed
+  pdl_trigger();
 
   const int num_m = (M + 2 * BM - 1) / (2 * BM), num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n;
@@ -864,9 +868,8 @@ static int launch(const void* A, long long lda, const void* B, long long ldb, vo
   if (st) return st;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_kernel<EPI, BN><<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                                                   M, N, K, qe, pe);
-  return check_launch("gemm_kernel");
+  return launch_pdl("gemm_kernel", gemm_kernel<EPI, BN>, dim3(grid), dim3(THREADS), C_::SMEM_BYTES, stream, ma, mb,
+                    reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe);
 }
 
 // Split-tile workspaces, one per (device, stream), registered by the caller (morj_gemm_workspace_set): the pair
@@ -923,9 +926,8 @@ static int launch2(const void* A, long long lda, const void* B, long long ldb, v
       sp.flags = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)pairs * kSlotBytesPerPair);
     }
   }
-  gemm2_kernel<EPI, BN><<<2 * clusters, THREADS, C_::SMEM_BYTES, stream>>>(
-      ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe, sp);
-  return check_launch("gemm2_kernel");
+  return launch_pdl("gemm2_kernel", gemm2_kernel<EPI, BN>, dim3(2 * clusters), dim3(THREADS), C_::SMEM_BYTES, stream,
+                    ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe, sp);
 }
 
 // Kernel and tile width: the smallest (waves x per-tile time) over the candidates. A wave is one tile per SM (one

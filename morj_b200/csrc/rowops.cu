@@ -38,6 +38,8 @@ __global__ void __launch_bounds__(THREADS) embed_rmsnorm_kernel(const int* __res
                                                                 float scale, const __nv_bfloat16* __restrict__ w,
                                                                 float eps, __nv_bfloat16* __restrict__ x_out,
                                                                 __nv_bfloat16* __restrict__ h_out) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   __shared__ float red[32];
   const size_t row = blockIdx.x;
   const int fr = feature_row ? feature_row[row] : -1;
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
                                                                 const __nv_bfloat16* __restrict__ w_post,
                                                                 const __nv_bfloat16* __restrict__ w_pre, int H,
                                                                 float eps) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   __shared__ float red[32];
   const size_t base = (size_t)blockIdx.x * H;
   float ov[VPT][8];
@@ -132,6 +136,8 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
                                                                const __nv_bfloat16* __restrict__ scalar,
                                                                const __nv_bfloat16* __restrict__ w_next, int H,
                                                                float eps, int has_next) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   __shared__ float red[32];
   const size_t base = (size_t)blockIdx.x * H;
   const float sc = __bfloat162float(scalar[0]);
@@ -193,6 +199,8 @@ __global__ void __launch_bounds__(THREADS) qkv_post_kernel(const __nv_bfloat16* 
                                                            __nv_bfloat16* __restrict__ q_out,
                                                            __nv_bfloat16* __restrict__ k_pool,
                                                            __nv_bfloat16* __restrict__ v_pool) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   constexpr int HALF = D / 2;
   constexpr int E = HALF / 32;
   const int tok = blockIdx.x;
@@ -251,6 +259,8 @@ __global__ void __launch_bounds__(THREADS) qkv_post_kernel(const __nv_bfloat16* 
 
 // ---- reference-layout GeGLU --------------------------------------------------------------------------------------
 __global__ void geglu_kernel(const __nv_bfloat16* __restrict__ gu, int F, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   const size_t row = blockIdx.y;
   for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8; c < F; c += gridDim.x * blockDim.x * 8) {
     float g[8], u[8], o[8];
@@ -266,6 +276,8 @@ __global__ void geglu_kernel(const __nv_bfloat16* __restrict__ gu, int F, __nv_b
 __global__ void copy_rows_kernel(const __nv_bfloat16* __restrict__ src, long long ld_src,
                                  const int* __restrict__ rows, int width, __nv_bfloat16* __restrict__ dst,
                                  long long ld_dst, int scatter) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   const int i = blockIdx.x;
   const size_t s = scatter ? (size_t)i : (size_t)rows[i];
   const size_t d = scatter ? (size_t)rows[i] : (size_t)i;
@@ -281,6 +293,8 @@ __global__ void __launch_bounds__(THREADS) label_head_kernel(const __nv_bfloat16
                                                              const __nv_bfloat16* __restrict__ norm_w,
                                                              const __nv_bfloat16* __restrict__ embed, int H,
                                                              float eps, float softcap, float* __restrict__ probs) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   extern __shared__ float sh[];
   float* normed = sh;      // H
   float* logits = sh + H;  // labels of this sequence
@@ -326,6 +340,8 @@ __global__ void __launch_bounds__(THREADS) label_head_kernel(const __nv_bfloat16
 // step (`f = positions * inv_freq`, `f.cos()`, `f.sin()`).
 __global__ void __launch_bounds__(256) rope_table_kernel(const float* __restrict__ inv_freq, int half, int rows,
                                                         float2* __restrict__ table) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)rows * half) return;
   const int p = (int)(i / half), f = (int)(i % half);
@@ -389,10 +405,13 @@ extern "C" int morj_embed_rmsnorm(const int* tokens, const int* feature_row, con
   if (!tokens || !embed || !norm_w || !x_out || !h_out || n < 0 || H <= 0 || H % 8 || (feature_row && !features))
     return set_error(MORJ_ERR_ARG, "morj_embed_rmsnorm: bad arguments (n=%d H=%d)", n, H);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  MORJ_VPT_SWITCH(H, (rows::embed_rmsnorm_kernel<V><<<n, rows::THREADS, 0, s>>>(
-                         tokens, feature_row, (const __nv_bfloat16*)features, (const __nv_bfloat16*)embed, H, scale,
-                         (const __nv_bfloat16*)norm_w, eps, (__nv_bfloat16*)x_out, (__nv_bfloat16*)h_out)));
-  return check_launch("embed_rmsnorm_kernel");
+  int st = MORJ_OK;
+  MORJ_VPT_SWITCH(H, (st = launch_pdl("embed_rmsnorm_kernel", rows::embed_rmsnorm_kernel<V>, dim3(n),
+                                      dim3(rows::THREADS), 0, s, tokens, feature_row,
+                                      (const __nv_bfloat16*)features, (const __nv_bfloat16*)embed, H, scale,
+                                      (const __nv_bfloat16*)norm_w, eps, (__nv_bfloat16*)x_out,
+                                      (__nv_bfloat16*)h_out)));
+  return st;
 }
 
 extern "C" int morj_attn_epilogue(const void* o, void* x, void* h_out, const void* w_post, const void* w_pre, int n,
@@ -401,10 +420,12 @@ extern "C" int morj_attn_epilogue(const void* o, void* x, void* h_out, const voi
   if (!o || !x || !h_out || !w_post || !w_pre || n < 0 || H <= 0 || H % 8)
     return set_error(MORJ_ERR_ARG, "morj_attn_epilogue: bad arguments (n=%d H=%d)", n, H);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  MORJ_VPT_SWITCH(H, (rows::attn_epilogue_kernel<V><<<n, rows::THREADS, 0, s>>>(
-                         (const __nv_bfloat16*)o, (__nv_bfloat16*)x, (__nv_bfloat16*)h_out,
-                         (const __nv_bfloat16*)w_post, (const __nv_bfloat16*)w_pre, H, eps)));
-  return check_launch("attn_epilogue_kernel");
+  int st = MORJ_OK;
+  MORJ_VPT_SWITCH(H, (st = launch_pdl("attn_epilogue_kernel", rows::attn_epilogue_kernel<V>, dim3(n),
+                                      dim3(rows::THREADS), 0, s, (const __nv_bfloat16*)o, (__nv_bfloat16*)x,
+                                      (__nv_bfloat16*)h_out, (const __nv_bfloat16*)w_post,
+                                      (const __nv_bfloat16*)w_pre, H, eps)));
+  return st;
 }
 
 extern "C" int morj_mlp_epilogue(const void* d, void* x, void* h_out, const void* w_post, const void* scalar,
@@ -413,11 +434,13 @@ extern "C" int morj_mlp_epilogue(const void* d, void* x, void* h_out, const void
   if (!d || !x || !w_post || !scalar || n < 0 || H <= 0 || H % 8 || (has_next && (!h_out || !w_next)))
     return set_error(MORJ_ERR_ARG, "morj_mlp_epilogue: bad arguments (n=%d H=%d)", n, H);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  MORJ_VPT_SWITCH(H, (rows::mlp_epilogue_kernel<V><<<n, rows::THREADS, 0, s>>>(
-                         (const __nv_bfloat16*)d, (__nv_bfloat16*)x, (__nv_bfloat16*)h_out,
-                         (const __nv_bfloat16*)w_post, (const __nv_bfloat16*)scalar, (const __nv_bfloat16*)w_next, H,
-                         eps, has_next)));
-  return check_launch("mlp_epilogue_kernel");
+  int st = MORJ_OK;
+  MORJ_VPT_SWITCH(H, (st = launch_pdl("mlp_epilogue_kernel", rows::mlp_epilogue_kernel<V>, dim3(n),
+                                      dim3(rows::THREADS), 0, s, (const __nv_bfloat16*)d, (__nv_bfloat16*)x,
+                                      (__nv_bfloat16*)h_out, (const __nv_bfloat16*)w_post,
+                                      (const __nv_bfloat16*)scalar, (const __nv_bfloat16*)w_next, H, eps,
+                                      has_next)));
+  return st;
 }
 
 extern "C" int morj_rope_table(const float* inv_freq, int half, int rows, void* table, void* stream) {
@@ -428,9 +451,8 @@ extern "C" int morj_rope_table(const float* inv_freq, int half, int rows, void* 
     return set_error(MORJ_ERR_ARG, "morj_rope_table: table must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long n = (long long)rows * half;
-  rows::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(inv_freq, half, rows,
-                                                                       reinterpret_cast<float2*>(table));
-  return check_launch("rope_table_kernel");
+  return launch_pdl("rope_table_kernel", rows::rope_table_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s,
+                    inv_freq, half, rows, reinterpret_cast<float2*>(table));
 }
 
 extern "C" int morj_qkv_post(const void* qkv, long long ld, int n, int hq, int hk, int has_v, int d,
@@ -446,19 +468,15 @@ extern "C" int morj_qkv_post(const void* qkv, long long ld, int n, int hq, int h
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(n, (heads + 7) / 8);
 #define MORJ_QKV(DD)                                                                                             \
-  rows::qkv_post_kernel<DD><<<grid, rows::THREADS, 0, s>>>(                                                      \
-      (const __nv_bfloat16*)qkv, ld, hq, hk, has_v, (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm,  \
-      positions, inv_freq, slots, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool, (__nv_bfloat16*)v_pool)
-  if (d == 64)
-    MORJ_QKV(64);
-  else if (d == 128)
-    MORJ_QKV(128);
-  else if (d == 256)
-    MORJ_QKV(256);
-  else
-    return set_error(MORJ_ERR_UNSUPPORTED, "morj_qkv_post: head_dim %d unsupported", d);
+  launch_pdl("qkv_post_kernel", rows::qkv_post_kernel<DD>, grid, dim3(rows::THREADS), 0, s,                      \
+             (const __nv_bfloat16*)qkv, ld, hq, hk, has_v, (const __nv_bfloat16*)q_norm,                          \
+             (const __nv_bfloat16*)k_norm, positions, inv_freq, slots, eps, (__nv_bfloat16*)q_out,                \
+             (__nv_bfloat16*)k_pool, (__nv_bfloat16*)v_pool)
+  if (d == 64) return MORJ_QKV(64);
+  if (d == 128) return MORJ_QKV(128);
+  if (d == 256) return MORJ_QKV(256);
 #undef MORJ_QKV
-  return check_launch("qkv_post_kernel");
+  return set_error(MORJ_ERR_UNSUPPORTED, "morj_qkv_post: head_dim %d unsupported", d);
 }
 
 extern "C" int morj_geglu(const void* gu, int n, int F, void* out, void* stream) {
@@ -466,8 +484,8 @@ extern "C" int morj_geglu(const void* gu, int n, int F, void* out, void* stream)
   if (!gu || !out || n < 0 || F <= 0 || F % 8) return set_error(MORJ_ERR_ARG, "morj_geglu: bad arguments");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid((F / 8 + 255) / 256, n);
-  rows::geglu_kernel<<<grid, 256, 0, s>>>((const __nv_bfloat16*)gu, F, (__nv_bfloat16*)out);
-  return check_launch("geglu_kernel");
+  return launch_pdl("geglu_kernel", rows::geglu_kernel, grid, dim3(256), 0, s, (const __nv_bfloat16*)gu, F,
+                    (__nv_bfloat16*)out);
 }
 
 static int copy_rows(const void* src, long long ld_src, const int* rows_, int n, int width, void* dst,
@@ -478,9 +496,8 @@ static int copy_rows(const void* src, long long ld_src, const int* rows_, int n,
     return set_error(MORJ_ERR_ARG, "morj row copy: bad arguments (n=%d width=%d)", n, width);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int threads = width / 8 < 256 ? ((width / 8 + 31) / 32) * 32 : 256;
-  rows::copy_rows_kernel<<<n, threads, 0, s>>>((const __nv_bfloat16*)src, ld_src, rows_, width, (__nv_bfloat16*)dst,
-                                               ld_dst, scatter);
-  return check_launch("copy_rows_kernel");
+  return launch_pdl("copy_rows_kernel", rows::copy_rows_kernel, dim3(n), dim3(threads), 0, s,
+                    (const __nv_bfloat16*)src, ld_src, rows_, width, (__nv_bfloat16*)dst, ld_dst, scatter);
 }
 
 extern "C" int morj_gather_rows(const void* src, long long ld_src, const int* rows_, int n, int width, void* dst,
@@ -510,8 +527,7 @@ extern "C" int morj_label_head(const void* x, long long ld_x, const int* seq_row
     configured = true;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  rows::label_head_kernel<<<n_seq, rows::THREADS, smem, s>>>((const __nv_bfloat16*)x, ld_x, seq_row, label_indptr,
-                                                             label_ids, (const __nv_bfloat16*)norm_w,
-                                                             (const __nv_bfloat16*)embed, H, eps, softcap, probs);
-  return check_launch("label_head_kernel");
+  return launch_pdl("label_head_kernel", rows::label_head_kernel, dim3(n_seq), dim3(rows::THREADS), smem, s,
+                    (const __nv_bfloat16*)x, ld_x, seq_row, label_indptr, label_ids, (const __nv_bfloat16*)norm_w,
+                    (const __nv_bfloat16*)embed, H, eps, softcap, probs);
 }

@@ -59,6 +59,8 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
                                                             const __nv_bfloat16* __restrict__ w_b, float eps,
                                                             int has_next, int push_x,
                                                             unsigned long long partial_target) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ int ok_s;
   const int H = p.hidden, world = p.world, rank = p.rank;
@@ -148,6 +150,8 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
 
 __global__ void __launch_bounds__(ROW_THREADS) wait_kernel(const unsigned long long* rows, int n_blocks,
                                                           unsigned long long target) {
+  pdl_wait();  // the previous kernel on the stream has completed
+  pdl_trigger();
   for (int b = threadIdx.x; b < n_blocks; b += ROW_THREADS)
     if (!wait_at_least(rows + b, target, kErrTimeoutPeerRows)) return;
 }
@@ -241,14 +245,17 @@ extern "C" int morj_peer_reduce(const morj_peer_t* p, int mode, int n, const voi
   const __nv_bfloat16* wa = static_cast<const __nv_bfloat16*>(w_a);
   const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(scalar);
   const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w_b);
+  int st2 = MORJ_OK;
   if (mode == 0) {
-    MORJ_VPT_SWITCH(H, (peer::reduce_kernel<V, 0><<<grid, ROW_THREADS, 0, s>>>(*p, n, wa, sc, wb, eps, 1, push_x,
-                                                                               partial_target)));
+    MORJ_VPT_SWITCH(H, (st2 = launch_pdl("peer::reduce_kernel", peer::reduce_kernel<V, 0>, dim3(grid),
+                                         dim3(ROW_THREADS), 0, s, *p, n, wa, sc, wb, eps, 1, push_x,
+                                         partial_target)));
   } else {
-    MORJ_VPT_SWITCH(H, (peer::reduce_kernel<V, 1><<<grid, ROW_THREADS, 0, s>>>(*p, n, wa, sc, wb, eps, has_next,
-                                                                               push_x, partial_target)));
+    MORJ_VPT_SWITCH(H, (st2 = launch_pdl("peer::reduce_kernel", peer::reduce_kernel<V, 1>, dim3(grid),
+                                         dim3(ROW_THREADS), 0, s, *p, n, wa, sc, wb, eps, has_next, push_x,
+                                         partial_target)));
   }
-  return check_launch("peer::reduce_kernel");
+  return st2;
 }
 
 extern "C" int morj_peer_wait(const morj_peer_t* p, int n, unsigned long long row_target, void* stream) {
@@ -257,6 +264,6 @@ extern "C" int morj_peer_wait(const morj_peer_t* p, int n, unsigned long long ro
   if (n < 0 || n > p->max_blocks * 128) return set_error(MORJ_ERR_ARG, "morj_peer_wait: n=%d out of range", n);
   if (n == 0) return MORJ_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  peer::wait_kernel<<<1, ROW_THREADS, 0, s>>>(p->rows[p->rank], (n + 127) / 128, row_target);
-  return check_launch("peer::wait_kernel");
+  return launch_pdl("peer::wait_kernel", peer::wait_kernel, dim3(1), dim3(ROW_THREADS), 0, s,
+                    (const unsigned long long*)p->rows[p->rank], (n + 127) / 128, row_target);
 }

@@ -170,8 +170,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 132);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int seg = work[2 * blockIdx.x], q0 = work[2 * blockIdx.x + 1];
-  const int h = blockIdx.y;
+  // CTAs run in grid order, so the KV head is the fast index: every head of the longest tile starts first
+  const int item = blockIdx.x / hk, h = blockIdx.x % hk;
+  const int seg = work[2 * item], q0 = work[2 * item + 1];
   const int G = hq / hk;
   const int QT = ROWS / G;
 
@@ -462,7 +463,7 @@ static int launch(const void* q, int n_q, const void* k_pool, const void* v_pool
     st = encode_tiled(&vm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v_pool, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
-  dim3 grid(n_work, hk);
+  dim3 grid(n_work * hk);  // (tile, KV head) pairs, longest tile first
   return launch_pdl("tree_attention_kernel", tree_attention_kernel<D>, grid, dim3(THREADS), Smem<D>::TOTAL, stream,
                     qm, km, vm, reinterpret_cast<const __nv_bfloat16*>(k_pool),
                     reinterpret_cast<const __nv_bfloat16*>(v_pool), reinterpret_cast<__nv_bfloat16*>(out), qo_indptr,

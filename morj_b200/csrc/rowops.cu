@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(THREADS) embed_rmsnorm_kernel(const int* __res
 }
 
 // ---- post-attention epilogue: x += rms(o) * w_post; h = rms(x) * w_pre -----------------------------------------
+// Both rows a CTA reads from HBM (o and x) are loaded up front and kept as packed BF16, so a row waits on HBM once;
+// the norm weights (shared by every row, L2-resident) are read where they are used.
 template <int VPT>
 __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloat16* __restrict__ o,
                                                                 __nv_bfloat16* __restrict__ x,
@@ -85,15 +87,24 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
   pdl_trigger();
   __shared__ float red[32];
   const size_t base = (size_t)blockIdx.x * H;
-  float ov[VPT][8];
+  uint4 o_raw[VPT], x_raw[VPT], w_raw[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = (threadIdx.x + k * THREADS) * 8;
+    if (c < H) {
+      o_raw[k] = *reinterpret_cast<const uint4*>(o + base + c);
+      x_raw[k] = *reinterpret_cast<const uint4*>(x + base + c);
+    }
+  }
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
     if (c < H) {
-      load8(o + base + c, ov[k]);
+      float ov[8];
+      unpack8(o_raw[k], ov);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += ov[k][e] * ov[k][e];
+      for (int e = 0; e < 8; ++e) ss += ov[e] * ov[e];
     }
   }
   const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
@@ -102,16 +113,19 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
     if (c < H) {
-      float xv[8], wv[8];
-      load8(x + base + c, xv);
+      float ov[8], xv[8], wv[8];
+      unpack8(o_raw[k], ov);
+      unpack8(x_raw[k], xv);
       load8(w_post + c, wv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float on = bf16_round(ov[k][e] * inv1 * wv[e]);
-        ov[k][e] = bf16_round(xv[e] + on);  // the new residual, reusing the registers
-        ss2 += ov[k][e] * ov[k][e];
+        const float on = bf16_round(ov[e] * inv1 * wv[e]);
+        xv[e] = bf16_round(xv[e] + on);  // the new residual
+        ss2 += xv[e] * xv[e];
       }
-      store8(x + base + c, ov[k]);
+      x_raw[k] = pack8(xv);
+      *reinterpret_cast<uint4*>(x + base + c) = x_raw[k];
+      w_raw[k] = *reinterpret_cast<const uint4*>(w_pre + c);
     }
   }
   const float inv2 = 1.0f / sqrtf(block_sum(ss2, red) / H + eps);
@@ -119,16 +133,18 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
     if (c < H) {
-      float wv[8], hv[8];
-      load8(w_pre + c, wv);
+      float xv[8], wv[8], hv[8];
+      unpack8(x_raw[k], xv);
+      unpack8(w_raw[k], wv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) hv[e] = ov[k][e] * inv2 * wv[e];
+      for (int e = 0; e < 8; ++e) hv[e] = xv[e] * inv2 * wv[e];
       store8(h_out + base + c, hv);
     }
   }
 }
 
 // ---- post-MLP epilogue: x = (x + rms(d) * w_post) * scalar; h = rms(x) * w_next ---------------------------------
+// d and x are loaded up front as in the post-attention epilogue.
 template <int VPT>
 __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat16* __restrict__ d,
                                                                __nv_bfloat16* x, __nv_bfloat16* h_out,
@@ -141,15 +157,24 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
   __shared__ float red[32];
   const size_t base = (size_t)blockIdx.x * H;
   const float sc = __bfloat162float(scalar[0]);
-  float dv[VPT][8];
+  uint4 d_raw[VPT], x_raw[VPT], w_raw[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = (threadIdx.x + k * THREADS) * 8;
+    if (c < H) {
+      d_raw[k] = *reinterpret_cast<const uint4*>(d + base + c);
+      x_raw[k] = *reinterpret_cast<const uint4*>(x + base + c);
+    }
+  }
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
     if (c < H) {
-      load8(d + base + c, dv[k]);
+      float dv[8];
+      unpack8(d_raw[k], dv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += dv[k][e] * dv[k][e];
+      for (int e = 0; e < 8; ++e) ss += dv[e] * dv[e];
     }
   }
   const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
@@ -158,17 +183,20 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
     if (c < H) {
-      float xv[8], wv[8];
-      load8(x + base + c, xv);
+      float dv[8], xv[8], wv[8];
+      unpack8(d_raw[k], dv);
+      unpack8(x_raw[k], xv);
       load8(w_post + c, wv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float dn = bf16_round(dv[k][e] * inv1 * wv[e]);
+        const float dn = bf16_round(dv[e] * inv1 * wv[e]);
         const float xa = bf16_round(xv[e] + dn);
-        dv[k][e] = bf16_round(xa * sc);
-        ss2 += dv[k][e] * dv[k][e];
+        xv[e] = bf16_round(xa * sc);
+        ss2 += xv[e] * xv[e];
       }
-      store8(x + base + c, dv[k]);
+      x_raw[k] = pack8(xv);
+      *reinterpret_cast<uint4*>(x + base + c) = x_raw[k];
+      if (has_next) w_raw[k] = *reinterpret_cast<const uint4*>(w_next + c);
     }
   }
   if (!has_next) return;
@@ -177,10 +205,11 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
     if (c < H) {
-      float wv[8], hv[8];
-      load8(w_next + c, wv);
+      float xv[8], wv[8], hv[8];
+      unpack8(x_raw[k], xv);
+      unpack8(w_raw[k], wv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) hv[e] = dv[k][e] * inv2 * wv[e];
+      for (int e = 0; e < 8; ++e) hv[e] = xv[e] * inv2 * wv[e];
       store8(h_out + base + c, hv);
     }
   }

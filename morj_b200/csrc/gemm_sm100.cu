@@ -378,6 +378,223 @@ MORJ_DEV void peer_arrive(unsigned long long*& count, unsigned long long cols, i
   count = nullptr;
 }
 
+// ---- epilogue stores through a per-warp shared-memory transpose (SM-pair kernel) ----
+// The accumulator gives each epilogue lane one row, so a direct 16-byte store per lane makes every store instruction
+// touch 32 rows: 32 L1 wavefronts and 32 partial-sector L2 writes, and on the last tile of a pair (the one whose
+// epilogue nothing overlaps) those stores cost up to 5-7 us per launch (measured by leaving them out). Here a
+// 64-column BF16 chunk (8 x 16 bytes per row) goes through the warp's 4 KB buffer: each lane writes its row
+// (128 bytes, 16-byte units XOR-swizzled by row & 7, so eight consecutive rows cover all 32 banks), then each of 8
+// read instructions takes 4 rows x 8 units and stores 4 whole 128-byte row segments. Measured: O projection 0.0695
+// -> 0.0666 ms, QKV with the head epilogue 0.1424 -> 0.1392 ms, down 0.3369 -> 0.3347 ms.
+constexpr int kStageBytesPerWarp = 32 * 128;
+
+MORJ_DEV void stage_st16(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+MORJ_DEV uint4 stage_ld16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Stores this warp's 32 rows x 64 BF16 columns (lane = row; v = the lane's 8 units of 8 columns). dst(r, u) gives
+// the address of unit u of warp row r, or nullptr to skip it.
+template <class Dst>
+MORJ_DEV void staged_store64(uint32_t buf, const uint4 (&v)[8], int lane, const Dst& dst) {
+  __syncwarp();  // the previous chunk's reads of the buffer are done
+#pragma unroll
+  for (int u = 0; u < 8; ++u) stage_st16(buf + lane * 128 + ((u ^ (lane & 7)) << 4), v[u]);
+  __syncwarp();
+  const int unit = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const uint4 val = stage_ld16(buf + r * 128 + ((unit ^ (r & 7)) << 4));
+    __nv_bfloat16* p = dst(r, unit);
+    if (p != nullptr) *reinterpret_cast<uint4*>(p) = val;
+  }
+}
+
+// BF16 store of this warp's 32 accumulator rows of tile column block n_blk (row_base = the warp's first row) into
+// C[row][n_blk * BN ...], rows below M and columns below N only.
+template <int BN>
+MORJ_DEV void store_rows_staged(uint32_t tacc, uint32_t buf, __nv_bfloat16* C, long long ldc, int row_base, int M,
+                                int n_blk, int N, int lane) {
+  const int lim = min(N, (n_blk + 1) * BN);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    uint32_t r0[32], r1[32];
+    tmem_ld32(tacc + c, r0);
+    tmem_ld32(tacc + c + 32, r1);  // (past BN only when BN % 64 != 0: accumulator columns left unstored)
+    tmem_wait_ld();
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t* r = u < 4 ? r0 : r1;
+      const int o = (u & 3) * 8;
+      v[u].x = pack_bf16x2(__uint_as_float(r[o + 0]), __uint_as_float(r[o + 1]));
+      v[u].y = pack_bf16x2(__uint_as_float(r[o + 2]), __uint_as_float(r[o + 3]));
+      v[u].z = pack_bf16x2(__uint_as_float(r[o + 4]), __uint_as_float(r[o + 5]));
+      v[u].w = pack_bf16x2(__uint_as_float(r[o + 6]), __uint_as_float(r[o + 7]));
+    }
+    const int col0 = n_blk * BN + c;
+    staged_store64(buf, v, lane, [&](int r, int u) -> __nv_bfloat16* {
+      const int row = row_base + r, col = col0 + u * 8;
+      return (row < M && col < lim) ? C + (size_t)row * ldc + col : nullptr;
+    });
+  }
+}
+
+// The head epilogue of the SM-pair kernel: the numerics of epilogue_qkv, with each head's D output columns of the
+// warp's 32 rows assembled in the warp's store buffer (D / 64 chunks of 32 rows x 128 bytes, units swizzled as in
+// staged_store64) and written 4 rows x 128 bytes per store instruction; each row's destination offset (its q row or
+// K / V pool slot) is shuffled to the lanes that store it.
+MORJ_DEV void stage_put32(uint32_t buf, int lane, int col, const float (&o)[32]) {
+  const uint32_t chunk = buf + (uint32_t)(col >> 6) * kStageBytesPerWarp + lane * 128;
+  const int unit0 = (col & 63) >> 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 v;
+    v.x = pack_bf16x2(o[i * 8 + 0], o[i * 8 + 1]);
+    v.y = pack_bf16x2(o[i * 8 + 2], o[i * 8 + 3]);
+    v.z = pack_bf16x2(o[i * 8 + 4], o[i * 8 + 5]);
+    v.w = pack_bf16x2(o[i * 8 + 6], o[i * 8 + 7]);
+    stage_st16(chunk + (((unit0 + i) ^ (lane & 7)) << 4), v);
+  }
+}
+
+// Writes the staged head (D columns of 32 rows) to base + off(row) for every row whose offset is >= 0.
+template <int D>
+MORJ_DEV void stage_flush_head(uint32_t buf, int lane, __nv_bfloat16* base, long long off) {
+  __syncwarp();
+  const int unit = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const long long o = __shfl_sync(0xffffffffu, off, r);
+#pragma unroll
+    for (int k = 0; k < D / 64; ++k) {
+      const uint4 val = stage_ld16(buf + k * kStageBytesPerWarp + r * 128 + ((unit ^ (r & 7)) << 4));
+      if (o >= 0) *reinterpret_cast<uint4*>(base + o + k * 64 + unit * 8) = val;
+    }
+  }
+}
+
+template <int BN, int D>
+MORJ_DEV void epilogue_qkv_staged(uint32_t tacc, uint32_t buf, int row, int n_blk, bool row_ok, const QkvEpi& e,
+                                  int N, int lane) {
+  static_assert(D % 64 == 0, "head width");
+  constexpr int HALF = D / 2;
+  const int n_heads = N / D;
+  int pos = row_ok ? e.positions[row] : 0;
+  if ((unsigned)pos >= (unsigned)e.rope_rows) {
+    if (row_ok) report(kErrBadIndex);
+    row_ok = false;
+    pos = 0;
+  }
+  const float4* rope = e.rope + (size_t)pos * (HALF / 2);
+  const long long slot = (row_ok && e.hk) ? (long long)e.slots[row] : 0;
+#pragma unroll 1
+  for (int hh = 0; hh < BN / D; ++hh) {
+    const int head = (n_blk * BN) / D + hh;
+    if (head >= n_heads) break;  // (warp-uniform)
+    const uint32_t tb = tacc + hh * D;
+    const bool is_q = head < e.hq;
+    const bool is_k = !is_q && head < e.hq + e.hk;
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tb + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float v = bf16_round(__uint_as_float(r[i]));
+        ss += v * v;
+      }
+    }
+    const float inv = 1.0f / sqrtf(ss / D + e.eps);
+    const __nv_bfloat16* w = is_q ? e.q_norm : e.k_norm;
+    __nv_bfloat16* base;
+    __nv_bfloat16* base_v = nullptr;  // full-attention layers: V is the unweighted norm of the K projection
+    long long off;
+    if (is_q) {
+      base = e.q_out;
+      off = ((long long)row * e.hq + head) * D;
+    } else if (is_k) {
+      base = e.k_pool;
+      off = (slot * e.hk + (head - e.hq)) * D;
+      if (!e.has_v) base_v = e.v_pool;
+    } else {
+      base = e.v_pool;
+      off = (slot * e.hk + (head - e.hq - e.hk)) * D;
+    }
+    if (!row_ok) off = -1;
+    __syncwarp();  // the previous head's flush has read the buffer
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 32) {
+      uint32_t r1[32], r2[32];
+      tmem_ld32(tb + c, r1);
+      tmem_ld32(tb + HALF + c, r2);
+      tmem_wait_ld();
+      float o1[32], o2[32];
+      if (is_q || is_k) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          float w1[8], w2[8];
+          unpack8_bf16(*reinterpret_cast<const uint4*>(w + c + j), w1);
+          unpack8_bf16(*reinterpret_cast<const uint4*>(w + HALF + c + j), w2);
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            const float4 cs = rope[(c + j + u) / 2];  // (cos, sin) of pairs c+j+u and c+j+u+1
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+              const int i = j + u + v;
+              const float co = v ? cs.z : cs.x, sn = v ? cs.w : cs.y;
+              const float a = bf16_round(__uint_as_float(r1[i])) * inv;
+              const float b = bf16_round(__uint_as_float(r2[i])) * inv;
+              const float y1 = bf16_round(a * w1[u + v]);  // rounded before RoPE, as the reference
+              const float y2 = bf16_round(b * w2[u + v]);
+              o1[i] = y1 * co - y2 * sn;
+              o2[i] = y2 * co + y1 * sn;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o1[i] = bf16_round(__uint_as_float(r1[i])) * inv;
+          o2[i] = bf16_round(__uint_as_float(r2[i])) * inv;
+        }
+      }
+      stage_put32(buf, lane, c, o1);
+      stage_put32(buf, lane, HALF + c, o2);
+    }
+    stage_flush_head<D>(buf, lane, base, off);
+    if (base_v != nullptr) {
+      __syncwarp();
+#pragma unroll 1
+      for (int c = 0; c < HALF; c += 32) {
+        uint32_t r1[32], r2[32];
+        tmem_ld32(tb + c, r1);
+        tmem_ld32(tb + HALF + c, r2);
+        tmem_wait_ld();
+        float o1[32], o2[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o1[i] = bf16_round(__uint_as_float(r1[i])) * inv;
+          o2[i] = bf16_round(__uint_as_float(r2[i])) * inv;
+        }
+        stage_put32(buf, lane, c, o1);
+        stage_put32(buf, lane, HALF + c, o2);
+      }
+      stage_flush_head<D>(buf, lane, base_v, off);
+    }
+  }
+}
+
 template <int EPI, int BN>
 MORJ_DEV void epilogue_tile(uint32_t tacc, int row, int n_blk, bool row_ok, __nv_bfloat16* C, long long ldc, int N) {
   if constexpr (EPI == MORJ_EPI_STORE) {
@@ -601,6 +818,20 @@ struct Cfg2 {
   static constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN);
 };
 
+// Store buffers of the pair kernel's four epilogue warps (after the stage ring): one 64-column chunk per warp for the
+// plain epilogue and the D = 64 head epilogue, a whole 128-column head for the D = 128 head epilogue, none for the
+// GeGLU and partial epilogues (direct stores).
+template <int EPI>
+constexpr int pair_stage_out_bytes() {
+  return EPI == MORJ_EPI_QKV_D128                                  ? 4 * 2 * kStageBytesPerWarp
+         : (EPI == MORJ_EPI_STORE || EPI == MORJ_EPI_QKV_D64) ? 4 * kStageBytesPerWarp
+                                                              : 0;
+}
+template <int EPI, int BN>
+constexpr int pair_smem_bytes() {
+  return Cfg2<BN>::SMEM_BYTES + pair_stage_out_bytes<EPI>();
+}
+
 template <int EPI, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -610,7 +841,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   constexpr int STAGES = C_::STAGES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  static_assert(pair_smem_bytes<EPI, BN>() <= 232448, "shared memory per CTA");
+  constexpr int STAGE_OUT = pair_stage_out_bytes<EPI>() / 4;  // per epilogue warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 4 * STAGE_OUT);
   // bars: full[STAGES] (used in CTA 0), empty[STAGES], acc_full[2], acc_empty[2] (used in CTA 0), done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -762,12 +995,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                                        sp.flags + slot - 8, lane, abort)) {
         break;
       } else if constexpr (EPI == MORJ_EPI_QKV_D128) {
-        epilogue_qkv<BN, 128>(tacc, row, tc.n, row < M, qe, N);
+        epilogue_qkv_staged<BN, 128>(tacc, smem_u32(smem) + STAGES * STAGE_BYTES + quarter * STAGE_OUT, row, tc.n,
+                                     row < M, qe, N, lane);
       } else if constexpr (EPI == MORJ_EPI_QKV_D64) {
-        epilogue_qkv<BN, 64>(tacc, row, tc.n, row < M, qe, N);
+        epilogue_qkv_staged<BN, 64>(tacc, smem_u32(smem) + STAGES * STAGE_BYTES + quarter * STAGE_OUT, row, tc.n,
+                                    row < M, qe, N, lane);
       } else if constexpr (EPI == EPI_PEER) {
         epilogue_peer<BN>(tacc, row, tc.n, M, N, pe, pend, pend_cols);
+      } else if constexpr (EPI == MORJ_EPI_STORE) {
+        store_rows_staged<BN>(tacc, smem_u32(smem) + STAGES * STAGE_BYTES + quarter * STAGE_OUT, C, ldc, row - lane,
+                              M, tc.n, N, lane);
       } else {
+        // GeGLU writes half as many columns per tile; staged, it measured 0.5% slower (255 registers), so its
+        // stores stay direct
         epilogue_tile<EPI, BN>(tacc, row, tc.n, row < M, C, ldc, N);
       }
       tc_fence_before();
@@ -906,7 +1146,7 @@ static int launch2(const void* A, long long lda, const void* B, long long ldb, v
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C_::SMEM_BYTES);
+                                         (pair_smem_bytes<EPI, BN>()));
     if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = true;
   }
@@ -926,7 +1166,7 @@ static int launch2(const void* A, long long lda, const void* B, long long ldb, v
       sp.flags = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)pairs * kSlotBytesPerPair);
     }
   }
-  return launch_pdl("gemm2_kernel", gemm2_kernel<EPI, BN>, dim3(2 * clusters), dim3(THREADS), C_::SMEM_BYTES, stream,
+  return launch_pdl("gemm2_kernel", gemm2_kernel<EPI, BN>, dim3(2 * clusters), dim3(THREADS), (pair_smem_bytes<EPI, BN>()), stream,
                     ma, mb, reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, qe, pe, sp);
 }
 

@@ -388,11 +388,17 @@ inline int vpt_for(int H) { return (H / 8 + ROW_THREADS - 1) / ROW_THREADS; }
     default: return set_error(MORJ_ERR_UNSUPPORTED, "hidden size %d above 16384", H); \
   }
 
-// tanh-approximated GELU from its definition 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+// GELU, tanh form, computed as the reference's GeGLU kernel computes it (FlashInfer `gelu_tanh_and_mul`,
+// `lean_core.py:685`): x * (0.5 * (1 + tanh(sqrt(2 / pi) * (x + 0.044715 x^3)))) with the hardware tanh approximation
+// (PTX `tanh.approx.f32`, one instruction).
+MORJ_DEV float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 MORJ_DEV float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float inner = k0 * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float cdf = 0.5f * (1.0f + tanh_approx(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+  return x * cdf;
 }
 
 // host side: status and the calling thread's last error message (rowops.cu)

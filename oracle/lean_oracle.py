@@ -26,6 +26,7 @@ import torch
 
 PREFIX = 'model.language_model.'
 BF = torch.bfloat16
+QUERY_BLOCK = 1024  # query rows per dense score block in `tree_attention`
 
 
 def _r(x, bf16):
@@ -123,14 +124,16 @@ def tree_attention(q, k_pool, v_pool, qo_indptr, kv_indptr, kv_indices, n_bidir,
         idx = torch.as_tensor(np.asarray(slots, dtype=np.int64))
         K = k_pool[idx].float()
         V = v_pool[idx].float()
-        Q = q[q0:q1].float()
         mask = segment_mask(q1 - q0, len(slots), window, s < n_bidir)
         Kg = K.repeat_interleave(G, dim=1)
         Vg = V.repeat_interleave(G, dim=1)
-        S = torch.einsum('qhd,khd->hqk', Q, Kg) * sm_scale
-        S = S.masked_fill(~mask[None], float('-inf'))
-        P = torch.softmax(S, -1)
-        out[q0:q1] = torch.einsum('hqk,khd->qhd', P, Vg)
+        # query blocks bound the score matrix (an 8,192-token segment would need hq x 8192^2 FP32 at once); each
+        # query row's softmax is over its own keys, so blocking changes nothing
+        for b0 in range(0, q1 - q0, QUERY_BLOCK):
+            b1 = min(q1 - q0, b0 + QUERY_BLOCK)
+            S = torch.einsum('qhd,khd->hqk', q[q0 + b0:q0 + b1].float(), Kg) * sm_scale
+            S = S.masked_fill(~mask[None, b0:b1], float('-inf'))
+            out[q0 + b0:q0 + b1] = torch.einsum('hqk,khd->qhd', torch.softmax(S, -1), Vg)
     return out
 
 
@@ -174,6 +177,45 @@ def label_probs(rows, norm_w, embed, labels, softcap, eps, bf16=True):
     return out
 
 
+def layer_from_state(g, i, kind):
+    """Layer i's weights in the reference's fused load layout (`lean_core.py:368-382`): `qkv` = [q; k(; v)], `gu` =
+    [gate; up], the layer scalar in BF16. `g(key)` returns a checkpoint tensor."""
+    p = f'{PREFIX}layers.{i}.'
+    a = p + 'self_attn.'
+    parts = [g(a + 'q_proj.weight'), g(a + 'k_proj.weight')]
+    if kind == 'sliding_attention':
+        parts.append(g(a + 'v_proj.weight'))
+    return dict(
+        kind=kind, qkv=torch.cat(parts, 0), o=g(a + 'o_proj.weight'),
+        gu=torch.cat([g(p + 'mlp.gate_proj.weight'), g(p + 'mlp.up_proj.weight')], 0),
+        down=g(p + 'mlp.down_proj.weight'), q_norm=g(a + 'q_norm.weight'), k_norm=g(a + 'k_norm.weight'),
+        in_ln=g(p + 'input_layernorm.weight'), post_attn=g(p + 'post_attention_layernorm.weight'),
+        pre_ff=g(p + 'pre_feedforward_layernorm.weight'), post_ff=g(p + 'post_feedforward_layernorm.weight'),
+        scalar=g(p + 'layer_scalar').to(BF))
+
+
+class StreamedLayers:
+    """A read-only list of layers fetched on demand, keeping only the two most recently used (a layer reads its own
+    weights and the next layer's input norm)."""
+
+    def __init__(self, n, fetch):
+        self.n, self.fetch, self.cache = n, fetch, {}
+
+    def __len__(self):
+        return self.n
+
+    def __getitem__(self, i):
+        if i < 0:
+            i += self.n
+        if not 0 <= i < self.n:
+            raise IndexError(i)
+        if i not in self.cache:
+            if len(self.cache) >= 2:
+                del self.cache[max(self.cache, key=lambda j: abs(j - i))]  # the farthest from i
+            self.cache[i] = self.fetch(i)
+        return self.cache[i]
+
+
 class OracleModel:
     """The decoder's weights from a state dict in the checkpoint key layout (`model.language_model.*`)."""
 
@@ -185,25 +227,25 @@ class OracleModel:
         self.geom = {'sliding_attention': (cfg['num_key_value_heads'], cfg['head_dim']),
                      'full_attention': (cfg['num_global_key_value_heads'], cfg['global_head_dim'])}
         self.image_id = top.get('image_token_id')
-        g = lambda k: state[k].cpu()
-        self.embed, self.norm = g(PREFIX + 'embed_tokens.weight'), g(PREFIX + 'norm.weight')
-        self.layers = []
-        for i, kind in enumerate(self.types):
-            p = f'{PREFIX}layers.{i}.'
-            a = p + 'self_attn.'
-            parts = [g(a + 'q_proj.weight'), g(a + 'k_proj.weight')]
-            if kind == 'sliding_attention':
-                parts.append(g(a + 'v_proj.weight'))
-            self.layers.append(dict(
-                kind=kind, qkv=torch.cat(parts, 0), o=g(a + 'o_proj.weight'),
-                gu=torch.cat([g(p + 'mlp.gate_proj.weight'), g(p + 'mlp.up_proj.weight')], 0),
-                down=g(p + 'mlp.down_proj.weight'), q_norm=g(a + 'q_norm.weight'), k_norm=g(a + 'k_norm.weight'),
-                in_ln=g(p + 'input_layernorm.weight'), post_attn=g(p + 'post_attention_layernorm.weight'),
-                pre_ff=g(p + 'pre_feedforward_layernorm.weight'), post_ff=g(p + 'post_feedforward_layernorm.weight'),
-                scalar=g(p + 'layer_scalar').to(BF)))
+        if state is None:  # `streamed`: the caller sets embed, norm and layers
+            self.embed = self.norm = self.layers = None
+        else:
+            g = lambda k: state[k].cpu()
+            self.embed, self.norm = g(PREFIX + 'embed_tokens.weight'), g(PREFIX + 'norm.weight')
+            self.layers = [layer_from_state(g, i, kind) for i, kind in enumerate(self.types)]
         self.inv = inv_freqs(cfg)
         # tensor-parallel check only: sums a row-parallel projection's partial output over ranks (None: one device)
         self.reduce = None
+
+    @classmethod
+    def streamed(cls, top, embed, norm, fetch):
+        """An oracle whose layers are fetched one at a time (`fetch(i)` -> the layer dict `layer_from_state` builds,
+        CPU tensors) and dropped after use: host memory holds the embedding and two layers, so a 60-layer 31B-class
+        forward fits in a few GB."""
+        self = cls(top, None)
+        self.embed, self.norm = embed.cpu(), norm.cpu()
+        self.layers = StreamedLayers(len(self.types), fetch)
+        return self
 
     def embed_rows(self, tokens, feature_rows=None, features=None, bf16=True):
         """embed[tok] * bf16(sqrt(H)) in BF16 (reference `lean_core.py:366,641`), or * sqrt(H) in FP32; image rows

@@ -77,3 +77,27 @@ def test_planted_mistake_in_the_oracle_is_caught(model, monkeypatch):
     monkeypatch.setattr(lo, 'attn_epilogue', skip_post_norm)
     got = flat(model.forward_tree(Tree, c['seqs'], c['label_ids'], 'bf16'))
     assert np.abs(got - flat(c['reference'][0])).max() > 2e-3
+
+
+def test_streamed_oracle_equals_the_resident_one(model):
+    """The layer-streamed form (used at the 60-layer 31B width) computes exactly what the resident form does, and
+    the dense attention's query blocking changes nothing."""
+    import oracle.lean_oracle as lo
+    c = CASES['tiny-nested']
+    top = model.top
+    state = random_state(top, seed=0)
+    fetched = []
+
+    def fetch(i):
+        fetched.append(i)
+        return lo.layer_from_state(lambda k: state[k], i, top['text_config']['layer_types'][i])
+    streamed = OracleModel.streamed(top, model.embed, model.norm, fetch)
+    want = flat(model.forward_tree(Tree, c['seqs'], c['label_ids'], 'bf16'))
+    assert np.array_equal(flat(streamed.forward_tree(Tree, c['seqs'], c['label_ids'], 'bf16')), want)
+    assert fetched == [0, 1]
+    lo.QUERY_BLOCK, saved = 7, lo.QUERY_BLOCK
+    try:
+        blocked = flat(model.forward_tree(Tree, c['seqs'], c['label_ids'], 'bf16'))
+    finally:
+        lo.QUERY_BLOCK = saved
+    assert np.abs(blocked - want).max() < 1e-6

@@ -46,7 +46,8 @@ def gelu_tanh(x):
 
 def rope_tables(positions, inv_freq):
     """cos/sin of positions * inv_freq in FP32 (reference `lean_core.py:636-640`)."""
-    f = torch.as_tensor(np.asarray(positions), dtype=torch.float32)[:, None] * inv_freq[None, :]
+    pos = torch.as_tensor(np.asarray(positions), dtype=torch.float32, device=inv_freq.device)
+    f = pos[:, None] * inv_freq[None, :]
     return f.cos(), f.sin()
 
 
@@ -83,12 +84,12 @@ def qkv_post(qkv, hq, hk, has_v, d, q_norm, k_norm, cos, sin, eps, bf16=True):
     return norm_rope(q, q_norm, True), norm_rope(k, k_norm, True), norm_rope(v, None, False)
 
 
-def segment_mask(q_len, kv_len, window, bidir):
+def segment_mask(q_len, kv_len, window, bidir, device=None):
     """[q_len, kv_len] visibility of a segment's keys (bottom-right aligned): causal, with the sliding window when
     window > 0; an image block (bidir) drops the causal bound and keeps its own block plus the window before each
     query (reference `lean_core.py:612-629` with FlashInfer's mask rules)."""
-    j = torch.arange(q_len)[:, None]
-    t = torch.arange(kv_len)[None, :]
+    j = torch.arange(q_len, device=device)[:, None]
+    t = torch.arange(kv_len, device=device)[None, :]
     diag = kv_len - q_len
     if bidir:
         lo = diag + torch.clamp(j - (window - 1), max=0) if window > 0 else torch.zeros_like(j)
@@ -106,7 +107,7 @@ def tree_attention(q, k_pool, v_pool, qo_indptr, kv_indptr, kv_indices, n_bidir,
     n, hq, d = q.shape
     hk = k_pool.shape[1]
     G = hq // hk
-    out = torch.zeros(n, hq, d, dtype=torch.float32)
+    out = torch.zeros(n, hq, d, dtype=torch.float32, device=q.device)
     qo = np.asarray(qo_indptr)
     kp = np.asarray(kv_indptr)
     ki = np.asarray(kv_indices)
@@ -121,10 +122,10 @@ def tree_attention(q, k_pool, v_pool, qo_indptr, kv_indptr, kv_indices, n_bidir,
             last = page_size if kv_last_page_len is None else int(kv_last_page_len[s])
             slots = np.concatenate([p * page_size + np.arange(page_size if i < len(pages) - 1 else last)
                                     for i, p in enumerate(pages)])
-        idx = torch.as_tensor(np.asarray(slots, dtype=np.int64))
+        idx = torch.as_tensor(np.asarray(slots, dtype=np.int64), device=k_pool.device)
         K = k_pool[idx].float()
         V = v_pool[idx].float()
-        mask = segment_mask(q1 - q0, len(slots), window, s < n_bidir)
+        mask = segment_mask(q1 - q0, len(slots), window, s < n_bidir, q.device)
         Kg = K.repeat_interleave(G, dim=1)
         Vg = V.repeat_interleave(G, dim=1)
         # query blocks bound the score matrix (an 8,192-token segment would need hq x 8192^2 FP32 at once); each
@@ -171,7 +172,7 @@ def label_probs(rows, norm_w, embed, labels, softcap, eps, bf16=True):
     out = []
     for r, ids in zip(rows, labels):
         normed = _r(rmsnorm(r[None], norm_w, eps), bf16)[0]
-        logits = normed.float() @ embed[torch.as_tensor(ids)].float().T
+        logits = normed.float() @ embed[torch.as_tensor(ids, device=embed.device)].float().T
         logits = softcap * torch.tanh(logits / softcap)
         out.append(torch.softmax(logits, -1).double().tolist())
     return out
@@ -217,9 +218,11 @@ class StreamedLayers:
 
 
 class OracleModel:
-    """The decoder's weights from a state dict in the checkpoint key layout (`model.language_model.*`)."""
+    """The decoder's weights from a state dict in the checkpoint key layout (`model.language_model.*`), on `device`
+    (the CPU by default; the same torch code runs on a CUDA device for full-size checks, where it goes through torch's
+    own library kernels, never this repository's)."""
 
-    def __init__(self, top, state):
+    def __init__(self, top, state, device='cpu'):
         cfg = top['text_config']
         self.top, self.cfg = top, cfg
         self.H, self.eps, self.softcap = cfg['hidden_size'], cfg['rms_norm_eps'], cfg['final_logit_softcapping']
@@ -227,36 +230,40 @@ class OracleModel:
         self.geom = {'sliding_attention': (cfg['num_key_value_heads'], cfg['head_dim']),
                      'full_attention': (cfg['num_global_key_value_heads'], cfg['global_head_dim'])}
         self.image_id = top.get('image_token_id')
+        self.device = torch.device(device)
         if state is None:  # `streamed`: the caller sets embed, norm and layers
             self.embed = self.norm = self.layers = None
         else:
-            g = lambda k: state[k].cpu()
+            g = lambda k: state[k].to(self.device)
             self.embed, self.norm = g(PREFIX + 'embed_tokens.weight'), g(PREFIX + 'norm.weight')
             self.layers = [layer_from_state(g, i, kind) for i, kind in enumerate(self.types)]
-        self.inv = inv_freqs(cfg)
+        self.inv = {k: v.to(self.device) for k, v in inv_freqs(cfg).items()}
         # tensor-parallel check only: sums a row-parallel projection's partial output over ranks (None: one device)
         self.reduce = None
 
     @classmethod
-    def streamed(cls, top, embed, norm, fetch):
+    def streamed(cls, top, embed, norm, fetch, device='cpu'):
         """An oracle whose layers are fetched one at a time (`fetch(i)` -> the layer dict `layer_from_state` builds,
         CPU tensors) and dropped after use: host memory holds the embedding and two layers, so a 60-layer 31B-class
         forward fits in a few GB."""
-        self = cls(top, None)
-        self.embed, self.norm = embed.cpu(), norm.cpu()
-        self.layers = StreamedLayers(len(self.types), fetch)
+        self = cls(top, None, device)
+        self.embed, self.norm = embed.to(self.device), norm.to(self.device)
+        self.layers = StreamedLayers(len(self.types), lambda i: {k: (v.to(self.device) if torch.is_tensor(v) else v)
+                                                                 for k, v in fetch(i).items()})
         return self
 
     def embed_rows(self, tokens, feature_rows=None, features=None, bf16=True):
         """embed[tok] * bf16(sqrt(H)) in BF16 (reference `lean_core.py:366,641`), or * sqrt(H) in FP32; image rows
         take their feature rows (reference `lean_core.py:642-650`)."""
         scale = float(torch.tensor(self.H ** 0.5, dtype=BF)) if bf16 else self.H ** 0.5
-        x = _r(self.embed[torch.as_tensor(np.asarray(tokens), dtype=torch.int64)].float() * scale, bf16)
+        x = _r(self.embed[torch.as_tensor(np.asarray(tokens), dtype=torch.int64, device=self.device)].float() * scale,
+               bf16)
         if feature_rows is not None:
             fr = np.asarray(feature_rows)
             rows = np.flatnonzero(fr >= 0)
             if len(rows):
-                x[torch.as_tensor(rows)] = features[torch.as_tensor(fr[rows])].float()
+                x[torch.as_tensor(rows, device=self.device)] = features.to(self.device)[
+                    torch.as_tensor(fr[rows], device=self.device)].float()
         return x
 
     def layer(self, i, x, h, st, cap, rope, pools=None, precision='bf16'):
@@ -272,13 +279,14 @@ class OracleModel:
         if pools is not None and pools[i] is not None:
             k_pool, v_pool = pools[i]
         else:
-            k_pool, v_pool = torch.zeros(cap[kk], hk, d), torch.zeros(cap[kk], hk, d)
+            k_pool = torch.zeros(cap[kk], hk, d, device=self.device)
+            v_pool = torch.zeros(cap[kk], hk, d, device=self.device)
             if pools is not None:
                 pools[i] = (k_pool, v_pool)
         cos, sin = rope[kind]
         qkv = _r(matmul(h, layer['qkv'], bf16), bf16)
         q, k, v = qkv_post(qkv, hq, hk, has_v, d, layer['q_norm'], layer['k_norm'], cos, sin, eps, bf16)
-        sl = torch.as_tensor(np.asarray(st['slots'][kk], dtype=np.int64))
+        sl = torch.as_tensor(np.asarray(st['slots'][kk], dtype=np.int64), device=self.device)
         k_pool[sl] = k
         v_pool[sl] = v
         window = self.window if kind == 'sliding_attention' else 0

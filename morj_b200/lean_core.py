@@ -35,58 +35,81 @@ MAX_LABELS = 8192  # labels per sequence the label-head kernel holds in shared m
 
 
 class Request:
-    """One request's tree, label ids, computed nodes and (with `retain`) its K/V pools
-    (reference `lean_core.py:323-336`)."""
+    """State of one scoring request across its passes. The attribute names are the ones `LeanEngine` and its stats
+    read (reference `lean_core.py:323-336`): `tree`, `label_ids` (per tree sequence; shape-only sequences get a dummy
+    label), `retain` (whole K/V kept for later passes), `pinned` (only the K/V later passes read kept), `head_nodes`
+    (nodes filled from the shared head, never computed), `computed` (nodes whose K/V are in the pools), `read`
+    (sequences already scored), `tables` (pinned mode: per kind, tree offset -> pool slot, -1 where dropped), `pools`
+    (per layer (K, V) while kept), `n_real` (the caller's sequences come first in the tree), `features` and
+    `bidir` (image blocks)."""
 
     def __init__(self, tree, label_ids, retain, head_nodes, pinned=False):
-        self.tree, self.label_ids, self.retain = tree, label_ids, retain
-        self.pinned = pinned
+        self.tree, self.label_ids = tree, label_ids
+        self.retain, self.pinned = retain, pinned
         self.head_nodes = head_nodes
         self.computed = set(head_nodes)
         self.read = set()
-        self.tables = None
-        self.pools = None
+        self.tables = self.pools = self.features = None
         self.n_real = len(tree.seqs)
-        self.features = None
         self.bidir = frozenset()
+        self.blocks = None
+
+
+class ImageBlocks:
+    """Where a request's images sit. Every image placeholder token becomes BOI, one image token per soft token, EOI
+    (the layout of reference `lean_core.py:433-444,471-484`); the blocks must lie in the prefix every sequence shares.
+
+    `seqs`: the expanded sequences; `splits`: prefixes of the first sequence ending at each block's first and last
+    token, which give every block its own tree nodes; `start`, `end`: each block's depth range; `off`: each block's
+    first row in the concatenated features."""
+
+    def __init__(self, seqs, images, image_id, boi_id, eoi_id):
+        sizes = np.asarray([len(f) for f in images], dtype=np.int64)
+        self.seqs = []
+        for seq in seqs:
+            arr = np.asarray(seq, dtype=np.int64)
+            marks = np.flatnonzero(arr == image_id)
+            if len(marks) != len(sizes):
+                raise ValueError(f'{len(sizes)} images but {len(marks)} image placeholders in a sequence')
+            pieces = np.split(arr, marks + 1)  # each piece but the last ends with its placeholder
+            out = []
+            for piece, n in zip(pieces, sizes):
+                out += piece[:-1].tolist() + [boi_id] + [image_id] * int(n) + [eoi_id]
+            out += pieces[-1].tolist()
+            self.seqs.append(out)
+        marks0 = np.flatnonzero(np.asarray(seqs[0]) == image_id)
+        # block k starts after its BOI; every earlier placeholder grew by its soft tokens + 1 (BOI and EOI replace it)
+        self.start = marks0 + 1 + np.concatenate([[0], np.cumsum(sizes + 1)[:-1]]).astype(np.int64)
+        self.end = self.start + sizes
+        self.off = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)
+        last = int(self.end[-1])
+        first = self.seqs[0]
+        if any(len(x) <= last or x[:last] != first[:last] for x in self.seqs):
+            raise ValueError('every branch must hold the same images in its shared prefix')
+        self.splits = [first[:int(e)] for pair in zip(self.start, self.end) for e in pair]
+
+    def bidir_nodes(self, tree):
+        """Nodes of the shared prefix that lie inside one image block (attended without the causal mask in sliding
+        layers)."""
+        inside = lambda s, e: bool(np.any((self.start <= s) & (e <= self.end)))
+        return frozenset(n for n in tree.paths[0] if inside(tree.nodes[n][1], tree.nodes[n][2]))
+
+    def feature_rows(self, tokens, positions, image_id):
+        """Per step token: its row in the concatenated image features, -1 for text tokens."""
+        rows = np.full(len(tokens), -1, np.int64)
+        img = np.flatnonzero(np.asarray(tokens) == image_id)
+        if len(img):
+            depth = np.asarray(positions)[img]
+            k = np.searchsorted(self.start, depth, side='right') - 1
+            if (k < 0).any() or (depth >= self.end[k]).any():
+                raise ValueError('image placeholder outside an image block')
+            rows[img] = self.off[k] + depth - self.start[k]
+        return rows
 
 
 def expand_images(seqs, images, image_id, boi_id, eoi_id):
-    """Image placeholders -> BOI + one image token per soft token + EOI; block bounds and the split sequences that
-    put node boundaries at every block's start and end (reference `lean_core.py:433-444,461-462,471-484`)."""
-    out = []
-    for seq in seqs:
-        exp, k = [], 0
-        for t in seq:
-            if t == image_id:
-                if k >= len(images):
-                    raise ValueError('more image placeholders than images')
-                exp += [boi_id] + [image_id] * len(images[k]) + [eoi_id]
-                k += 1
-            else:
-                exp.append(t)
-        if k != len(images):
-            raise ValueError(f'{len(images)} images but {k} placeholders')
-        out.append(exp)
-    first = np.asarray(out[0])
-    run_start = (first == image_id) & np.r_[True, first[:-1] != image_id]
-    starts = np.flatnonzero(run_start)
-    blobs = [(int(s), int(s) + len(f)) for s, f in zip(starts, images)]
-    end = blobs[-1][1]
-    if any(len(s) <= end or s[:end] != out[0][:end] for s in out):
-        raise ValueError('every branch must hold the same images in its shared prefix')
-    splits = []
-    for s, e in blobs:
-        splits += [out[0][:s], out[0][:e]]
-    blob_start = np.asarray([s for s, _ in blobs])
-    blob_end = np.asarray([e for _, e in blobs])
-    blob_off = np.concatenate([[0], np.cumsum([e - s for s, e in blobs])])[:-1]
-
-    def bidir_nodes(tree):
-        return frozenset(n for n in tree.paths[0]
-                         if any(s <= tree.nodes[n][1] and tree.nodes[n][2] <= e for s, e in blobs))
-    return dict(seqs=out, splits=splits, blob_start=blob_start, blob_end=blob_end, blob_off=blob_off,
-                bidir_nodes=bidir_nodes)
+    """The image layout of a request (see `ImageBlocks`)."""
+    return ImageBlocks(seqs, images, image_id, boi_id, eoi_id)
 
 
 def interleave_glu(gate, up, block=GLU_BLOCK):
@@ -262,88 +285,103 @@ class LeanGemma4:
 
     # ---- requests -------------------------------------------------------------------------------------------------
     def set_shared_prefix(self, tokens):
-        """Compute and keep the K/V of a prefix many requests start with (reference `lean_core.py:419-426`)."""
-        self.shared, self.shared_kv = None, None
+        """Compute a prefix that many requests start with once, and keep its K/V: every later request whose sequences
+        all start with it gets the K/V copied into its head slots instead of computed (`lean_core.py:419-426`)."""
+        self.shared = self.shared_kv = None
         req = self.prepare([list(tokens)], [[0]], retain=True)
         self.run(req, [0])
-        self.shared = np.asarray(tokens, dtype=np.int64)
-        slots = np.concatenate([req.tree.slots(n) for n in req.tree.paths[0]])
-        idx = torch.as_tensor(slots.astype(np.int32), device=self.device)
+        offsets = np.concatenate([req.tree.slots(n) for n in req.tree.paths[0]]).astype(np.int32)
+        idx = torch.as_tensor(offsets, device=self.device)
         kv = [(self._gather(k, idx), self._gather(v, idx)) for k, v in req.pools]
         torch.cuda.current_stream(self.device).synchronize()
-        self.shared_kv = kv
+        self.shared, self.shared_kv = np.asarray(tokens, dtype=np.int64), kv
+
+    def _starts_with_shared(self, seqs):
+        n = 0 if self.shared is None else len(self.shared)
+        return bool(n) and bool(seqs) and all(len(x) > n and np.array_equal(x[:n], self.shared) for x in seqs)
+
+    def _retention(self, tokens, retain, available):
+        """(keep whole, keep pinned) for a request of `tokens` tree tokens. A retained request keeps all its K/V when
+        they fit both the retention budget and the memory left after one step's activations; otherwise it keeps only
+        what its later passes read (the reference's rule, `lean_core.py:451-454`, which the adapter's OOM ladder
+        relies on)."""
+        if not retain:
+            return False, False
+        room = (self.free_bytes if available is None else available) - min(tokens, self.single_max) * self.act_bytes
+        whole = tokens * self.kv_bytes <= min(self.retain_budget, room)
+        return whole, not whole
 
     def prepare(self, seqs, label_ids, retain=False, images=None, available=None):
-        """A request over `seqs` (reference `lean_core.py:428-469`): the tree (with image blocks expanded and split,
-        and the shared head attached when every sequence starts with it), the retention decision, and retained
-        pools with the shared head's K/V copied in."""
-        seqs = [list(s) for s in seqs]
-        splits, layout = [], None
-        if images:
-            layout = expand_images(seqs, images, self.image_id, self.boi_id, self.eoi_id)
-            seqs, splits = layout['seqs'], layout['splits']
-        shared = self.shared is not None and len(seqs) and all(
-            len(s) > len(self.shared) and np.array_equal(np.asarray(s[:len(self.shared)]), self.shared) for s in seqs)
-        tree = Tree(seqs + splits + ([self.shared] if shared else []))
-        head = tree.paths[-1] if shared else []
-        avail = self.free_bytes if available is None else available
-        fits = tree.num_tokens * self.kv_bytes <= min(
-            self.retain_budget, avail - min(tree.num_tokens, self.single_max) * self.act_bytes)
-        req = Request(tree, list(label_ids) + [[0]] * len(splits) + ([[0]] if shared else []), retain and fits, head,
-                      pinned=retain and not fits)
+        """A request over `seqs`, every sequence it may score (`lean_core.py:428-469`): image placeholders expanded,
+        the tree (with extra shape-only sequences: image-block bounds, the shared head), the retention decision, and
+        for a request kept whole its pools with the shared head's K/V in place."""
+        seqs = [list(x) for x in seqs]
+        blocks = ImageBlocks(seqs, images, self.image_id, self.boi_id, self.eoi_id) if images else None
+        if blocks is not None:
+            seqs = blocks.seqs
+        shared = self._starts_with_shared(seqs)
+        shape_only = (blocks.splits if blocks is not None else []) + ([self.shared] if shared else [])
+        tree = Tree(seqs + shape_only)
+        whole, pinned = self._retention(tree.num_tokens, retain, available)
+        req = Request(tree, list(label_ids) + [[0]] * len(shape_only), whole, tree.paths[-1] if shared else [],
+                      pinned=pinned)
         req.n_real = len(seqs)
-        if images:
+        if blocks is not None:
+            req.blocks = blocks
             req.features = torch.cat([f.to(self.device, torch.bfloat16) for f in images]).contiguous()
-            req.blob_start, req.blob_end, req.blob_off = layout['blob_start'], layout['blob_end'], layout['blob_off']
-            req.bidir = layout['bidir_nodes'](tree)
-        if req.retain:
-            req.pools = [self._pool(kind, tree.num_tokens) for kind in self.types]
+            req.bidir = blocks.bidir_nodes(tree)
+        if whole:
+            req.pools = [self._kv_pool(kind, tree.num_tokens) for kind in self.types]
             if shared:
-                head_slots = np.concatenate([tree.slots(n) for n in head])
-                for (k, v), (sk, sv) in zip(req.pools, self.shared_kv):
-                    self._fill_head(k, v, head_slots, sk, sv)
+                self._copy_head(req.pools, None, np.concatenate([tree.slots(n) for n in req.head_nodes]))
         return req
 
-    def _pool(self, kind, n):
+    def _kv_pool(self, kind, slots):
+        """A (K, V) pair of `slots` rows for one layer of `kind`. With POISON (tests) every row starts as NaN."""
         hk, d = self.geom[kind]
-        shape = (max(n, 1), hk, d)
-        if POISON:  # test only: a slot read before it is written turns the answer into NaN
-            return (torch.full(shape, float('nan'), dtype=torch.bfloat16, device=self.device),
-                    torch.full(shape, float('nan'), dtype=torch.bfloat16, device=self.device))
-        return (torch.empty(shape, dtype=torch.bfloat16, device=self.device),
-                torch.empty(shape, dtype=torch.bfloat16, device=self.device))
+        shape = (max(slots, 1), hk, d)
+        if POISON:
+            return tuple(torch.full(shape, float('nan'), dtype=torch.bfloat16, device=self.device) for _ in 'kv')
+        return tuple(torch.empty(shape, dtype=torch.bfloat16, device=self.device) for _ in 'kv')
 
     def _gather(self, src, idx):
+        """Rows `idx` of a pool, as a new tensor (native row copy)."""
         width = src[0].numel()
         out = torch.empty((len(idx),) + tuple(src.shape[1:]), dtype=src.dtype, device=self.device)
-        self._k('rows', 'morj_gather_rows', src.data_ptr(), width, idx.data_ptr(), len(idx), width, out.data_ptr(), width,
-                 self._stream())
+        self._k('rows', 'morj_gather_rows', src.data_ptr(), width, idx.data_ptr(), len(idx), width, out.data_ptr(),
+                width, self._stream())
         return out
 
-    def _fill_head(self, k, v, slots, sk, sv):
-        """Copy the shared head's K/V rows into pool slots (reference `lean_core.py:594-597`)."""
-        idx = torch.as_tensor(np.asarray(slots, dtype=np.int32), device=self.device)
-        width = k[0].numel()
-        for dst, src in ((k, sk), (v, sv)):
-            nat.call('morj_scatter_rows', src.data_ptr(), width, idx.data_ptr(), len(idx), width, dst.data_ptr(),
-                     width, self._stream())
+    def _copy_head(self, pools, slot_of, head, layers=None):
+        """The shared head's K/V into the pools of `layers` (default every layer, `pools[j]` for layer `layers[j]`),
+        at the head's slots: the tree offsets `head` mapped through `slot_of` (per kind; None when slots are tree
+        offsets) (`lean_core.py:594-597`)."""
+        for (k, v), i in zip(pools, layers if layers is not None else range(len(self.types))):
+            slots = head if slot_of is None else slot_of[KINDS[self.types[i]]][head]
+            idx = torch.as_tensor(np.asarray(slots, dtype=np.int32), device=self.device)
+            width = k[0].numel()
+            for dst, src in zip((k, v), self.shared_kv[i]):
+                nat.call('morj_scatter_rows', src.data_ptr(), width, idx.data_ptr(), len(idx), width, dst.data_ptr(),
+                         width, self._stream())
 
-    def _grow(self, req, cap, kinds):
-        """Pinned-mode pools with at least `cap` slots per kind; existing slots keep their contents
-        (reference `lean_core.py:578-592`)."""
+    def _grow(self, req, cap):
+        """A pinned request's pools, enlarged to at least `cap` slots per kind when a pass needs more; the rows held so
+        far move to the same slots of the new pools (`lean_core.py:578-592`)."""
         old = req.pools
-        if old is not None and all(old[i][0].shape[0] >= cap[kinds[k]] for i, k in enumerate(self.types)):
+        short = old is None or any(old[i][0].shape[0] < cap[KINDS[kind]] for i, kind in enumerate(self.types))
+        if not short:
             return old
-        pools = []
-        for i, kind in enumerate(self.types):
-            k, v = self._pool(kind, cap[kinds[kind]])
-            if old is not None:
-                n = min(old[i][0].shape[0], k.shape[0])
-                k[:n].copy_(old[i][0][:n])
-                v[:n].copy_(old[i][1][:n])
-            pools.append((k, v))
-        req.pools = pools
-        return pools
+        new = [self._kv_pool(kind, cap[KINDS[kind]]) for kind in self.types]
+        if old is not None:
+            for (k, v), (ok, ov) in zip(new, old):
+                n = min(ok.shape[0], k.shape[0])
+                idx = torch.arange(n, dtype=torch.int32, device=self.device)
+                width = k[0].numel()
+                for dst, src in ((k, ok), (v, ov)):
+                    nat.call('morj_gather_rows', src.data_ptr(), width, idx.data_ptr(), n, width, dst.data_ptr(),
+                             width, self._stream())
+        req.pools = new
+        return new
 
     def _stream(self):
         s = torch.cuda.current_stream(self.device).cuda_stream
@@ -352,115 +390,131 @@ class LeanGemma4:
         return s
 
     # ---- pass -----------------------------------------------------------------------------------------------------
+    def _pass_bytes(self, plan, persistent):
+        """Device bytes a planned pass needs: its largest step's activations, plus every layer's pools when they live
+        for the whole pass (pinned requests, and multi-step passes of requests not kept whole)."""
+        largest = max(len(st['tokens']) for st in plan['steps'])
+        pools = sum(plan['cap'][KINDS[t]] * 4 * self.geom[t][0] * self.geom[t][1] for t in self.types)
+        return (pools if persistent else 0) + largest * self.act_bytes
+
     def plan(self, req, seqs, available=None):
-        """The planning half of `run` (reference `lean_core.py:497-529`): nodes to compute, pinned offsets and the
-        pass plan after the memory-fit loop (raises MemoryError when nothing fits). No device work."""
+        """The planning half of `run` (`lean_core.py:497-529`): the nodes to compute, the head's tree offsets, the
+        pinned offsets, and a plan whose memory fits `available` (default `free_bytes`).
+
+        Fitting: the whole pass as one step first; then in steps of `step_tokens` (so a pass's sliding-window slots
+        are reused as it moves on); then steps halved down to 512 tokens, below which the request does not fit and
+        MemoryError is raised (the adapter then frees memory and retries)."""
         tree = req.tree
-        cached = req.computed if req.retain or req.pinned else set(req.head_nodes)
+        cached = req.computed if (req.retain or req.pinned) else set(req.head_nodes)
         need = tree.pass_nodes(seqs, cached)
-        per_token = {kk: sum(4 * self.geom[k][0] * self.geom[k][1] for k in self.types if KINDS[k] == kk)
-                     for kk in 'gs'}
-        head = np.concatenate([tree.slots(n) for n in req.head_nodes]) if req.head_nodes else np.zeros(0, np.int64)
+        head = (np.concatenate([tree.slots(n) for n in req.head_nodes]) if req.head_nodes
+                else np.zeros(0, np.int64))
         pinned = None
         if req.pinned:
-            future = [b for b in range(req.n_real) if b not in req.read and b not in set(seqs)]
-            pinned = tree.pinned_for(cached | set(need), future, self.window)
-        step, single = self.step_tokens, self.single_max
+            later = [b for b in range(req.n_real) if b not in req.read and b not in set(seqs)]
+            pinned = tree.pinned_for(cached | set(need), later, self.window)
+        budget = self.free_bytes if available is None else available
+        single, step = self.single_max, self.step_tokens
         while True:
             plan = tree.plan_pass(need, seqs, self.window, single, step, req.retain,
                                   prealloc=() if req.retain else head, initial=req.tables, pinned=pinned,
                                   bidir=req.bidir)
-            multi = len(plan['steps']) > 1
-            persistent = req.pinned or (multi and not req.retain)
-            largest = max(len(st['tokens']) for st in plan['steps'])
-            pools = sum(plan['cap'][kk] * per_token[kk] for kk in 'gs') if persistent else 0
-            budget = self.free_bytes if available is None else available
-            if pools + largest * self.act_bytes <= budget:
-                break
+            one_step = len(plan['steps']) == 1
+            cost = self._pass_bytes(plan, req.pinned or (not one_step and not req.retain))
+            if cost <= budget:
+                return need, head, pinned, plan
             if step <= 512:
-                raise MemoryError(f'request needs {pools / 2**30:.1f} GiB of K/V pools; '
-                                  f'{budget / 2**30:.1f} GiB available')
-            if not multi and single:
-                single = 0  # pools for every layer at once: cut the pass into steps so slots are freed as it goes
+                raise MemoryError(f'the pass needs {cost / 2**30:.2f} GiB at 512-token steps; '
+                                  f'{budget / 2**30:.2f} GiB available')
+            if one_step and single:
+                single = 0
             else:
                 step //= 2
-        return need, head, pinned, plan
+
+    def _pass_pools(self, req, plan, head):
+        """The pools a pass writes: the request's own (kept whole, or pinned and grown as needed), fresh pools for
+        every layer when a pass of several steps must keep K/V between its steps, or None when one step runs with a
+        temporary pool per layer kind. New pools get the shared head's K/V."""
+        if req.retain:
+            return req.pools
+        if req.pinned:
+            pools, fresh = self._grow(req, plan['cap']), req.tables is None
+        elif len(plan['steps']) > 1:
+            pools, fresh = [self._kv_pool(kind, plan['cap'][KINDS[kind]]) for kind in self.types], True
+        else:
+            return None
+        if fresh and len(head):
+            self._copy_head(pools, plan['slot_of'], head)
+        return pools
 
     def prepare_pass(self, req, seqs, available=None):
-        """Host half of `run`: plan (with the memory-fit loop), the pools the pass writes (retained, pinned, per-pass,
-        or per-step temporaries), and every step's tables uploaded to the device. The result can be executed any
-        number of times (`execute_pass`); each execution recomputes the same nodes into the same slots."""
-        tree = req.tree
+        """Host half of `run`: plan (with the memory fit), the pools the pass writes, and every step's tables uploaded
+        to the device. The result can be executed any number of times (`execute_pass`); each execution recomputes
+        the same nodes into the same slots."""
         t0 = time.perf_counter()
         need, head, pinned, plan = self.plan(req, seqs, available)
-        multi = len(plan['steps']) > 1
-        if req.retain:
-            pools = req.pools
-        elif req.pinned:  # pools kept for the request; grown (old slots copied) when a pass needs more
-            pools = self._grow(req, plan['cap'], KINDS)
-            if req.tables is None and len(head):
-                for i, (k, v) in enumerate(pools):
-                    self._fill_head(k, v, plan['slot_of'][KINDS[self.types[i]]][head], *self.shared_kv[i])
-        elif multi:  # pools for the pass, every layer
-            pools = [self._pool(kind, plan['cap'][KINDS[kind]]) for kind in self.types]
-            if len(head):
-                for i, (k, v) in enumerate(pools):
-                    self._fill_head(k, v, plan['slot_of'][KINDS[self.types[i]]][head], *self.shared_kv[i])
-        else:
-            pools = None  # one forward: a temporary pool per kind
+        pools = self._pass_pools(req, plan, head)
         labels = [req.label_ids[b] for b in seqs]
         if any(len(ids) > MAX_LABELS for ids in labels):
             raise ValueError(f'at most {MAX_LABELS} labels per sequence')
         self.h2d_bytes = 0
         tables = [self._step_tables(k, st, plan, req) for k, st in enumerate(plan['steps'])]
         ro = self._readout_tables(plan, labels)
-        host_ms = 1000 * (time.perf_counter() - t0)
         return dict(req=req, seqs=list(seqs), need=need, head=head, pinned=pinned, plan=plan, pools=pools,
-                    labels=labels, tables=tables, ro=ro, host_ms=host_ms, h2d_bytes=self.h2d_bytes,
-                    tokens=sum(len(st['tokens']) for st in plan['steps']))
+                    labels=labels, tables=tables, ro=ro, host_ms=1000 * (time.perf_counter() - t0),
+                    h2d_bytes=self.h2d_bytes, tokens=sum(len(st['tokens']) for st in plan['steps']))
 
     def execute_pass(self, p):
         """Device half of `run`: every step's forward and the label head; returns the FP32 probabilities (device,
         CSR over the requested sequences' labels). Launches only; nothing waits for the GPU."""
         plan = p['plan']
-        finals = [self._step(k, st, plan, p['pools'], p['head'], p['req'], p['tables'][k])
-                  for k, st in enumerate(plan['steps'])]
-        return self._readout(finals, p['ro'])
+        if self.peer is not None:
+            self.peer.begin_pass()
+        reads = torch.empty(len(plan['readout']), self.hidden, dtype=torch.bfloat16, device=self.device)
+        at = 0
+        for k, st in enumerate(plan['steps']):
+            n_rows = len(p['tables'][k][1])
+            self._step(k, st, plan, p['pools'], p['head'], p['req'], p['tables'][k], reads[at:at + n_rows])
+            at += n_rows
+        return self._readout(reads[:at], p['ro'])
+
+    def _finish_pass(self, req, p):
+        """What a finished pass leaves in the request: the sequences read, the nodes whose K/V are now kept, and in
+        pinned mode the slot of every kept offset for the next pass's plan (`lean_core.py:565-575`)."""
+        req.read.update(p['seqs'])
+        if req.retain or req.pinned:
+            req.computed.update(p['need'])
+        if req.pinned:
+            n, plan, pinned = req.tree.num_tokens, p['plan'], p['pinned']
+            req.tables = {}
+            for kk in 'gs':
+                table = np.full(n, -1)
+                table[pinned[kk]] = plan['slot_of'][kk][pinned[kk]]
+                req.tables[kk] = table
 
     @torch.inference_mode()
     def run(self, req, seqs, available=None):
-        """Label probabilities for sequences `seqs` of `req`, computing only the nodes not cached yet
-        (reference `lean_core.py:495-576`: the same planning, memory-fit loop, pool strategy and state updates)."""
-        tree = req.tree
+        """Label probabilities of sequences `seqs` of `req`, computing only the nodes it has not kept yet
+        (`lean_core.py:495-576`): one list per sequence, in order, each the softmax over that sequence's labels."""
         p = self.prepare_pass(req, seqs, available)
         self.last_need = p['need']
-        plan, pinned, labels = p['plan'], p['pinned'], p['labels']
-        self.timing = {'host_setup_ms': p['host_ms'], 'steps': len(plan['steps']), 'tokens': p['tokens']}
+        self.timing = {'host_setup_ms': p['host_ms'], 'steps': len(p['plan']['steps']), 'tokens': p['tokens']}
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         probs = self.execute_pass(p)
         end.record()
-        self.enqueued = time.perf_counter()  # host done launching; the copy below waits for the GPU
+        self.enqueued = time.perf_counter()  # every launch queued; the copy below waits for the GPU
         flat = probs.cpu().numpy()
         self.d2h_bytes = flat.nbytes
         code = nat.device_error(self._stream())
+        if self.peer is not None:
+            code = self.peer.end_pass(code)
         if code:
             raise nat.NativeFailure(f'a kernel reported device error 0x{code:x}')
-        out, o = [], 0
-        for ids in labels:
-            out.append(flat[o:o + len(ids)].astype(np.float64).tolist())
-            o += len(ids)
-        self.gpu_ms = start.elapsed_time(end)
-        self.timing['gpu_ms'] = self.gpu_ms
-        req.read.update(seqs)
-        if req.retain or req.pinned:
-            req.computed.update(p['need'])
-        if req.pinned:
-            req.tables = {}
-            for kk in 'gs':
-                table = np.full(tree.num_tokens, -1)
-                table[pinned[kk]] = plan['slot_of'][kk][pinned[kk]]
-                req.tables[kk] = table
+        bounds = np.cumsum([0] + [len(ids) for ids in p['labels']])
+        out = [flat[a:b].astype(np.float64).tolist() for a, b in zip(bounds[:-1], bounds[1:])]
+        self.gpu_ms = self.timing['gpu_ms'] = start.elapsed_time(end)
+        self._finish_pass(req, p)
         return out
 
     def _readout_tables(self, plan, labels):
@@ -480,14 +534,12 @@ class LeanGemma4:
         self.h2d_bytes += t.nbytes
         return dict(t=t, n_seq=len(labels), n_labels=int(indptr[-1]))
 
-    def _readout(self, finals, ro):
-        """Final norm + label rows + softcap + per-sequence softmax in one kernel (reference `lean_core.py:558-561`)."""
-        H = self.hidden
-        xs = [xr for xr, rows in finals if rows]
-        x_all = xs[0] if len(xs) == 1 else torch.cat(xs)
-        t = ro['t']
+    def _readout(self, reads, ro):
+        """Final norm + label rows + softcap + per-sequence softmax in one kernel (`lean_core.py:558-561`) over the
+        readout rows of every step (`reads`, in step order)."""
+        H, t = self.hidden, ro['t']
         probs = torch.empty(ro['n_labels'], dtype=torch.float32, device=self.device)
-        self._k('head', 'morj_label_head', x_all.data_ptr(), H, t.ptr('seq_row'), t.ptr('indptr'), t.ptr('labels'),
+        self._k('head', 'morj_label_head', reads.data_ptr(), H, t.ptr('seq_row'), t.ptr('indptr'), t.ptr('labels'),
                 ro['n_seq'], self.norm.data_ptr(), self.embed.data_ptr(), H, self.eps, self.softcap,
                 probs.data_ptr(), self._stream())
         return probs
@@ -524,15 +576,7 @@ class LeanGemma4:
             t.add('work_' + kk, w)
             n_work[kk] = len(w) // 2
         if req.features is not None:
-            rows = np.flatnonzero(st['tokens'] == self.image_id)
-            fr = np.full(n, -1, np.int64)
-            if len(rows):
-                depth = st['positions'][rows]
-                kb = np.searchsorted(req.blob_start, depth, side='right') - 1
-                if (kb < 0).any() or (depth >= req.blob_end[kb]).any():
-                    raise ValueError('image placeholder outside an image block')
-                fr[rows] = req.blob_off[kb] + depth - req.blob_start[kb]
-            t.add('feature_row', fr)
+            t.add('feature_row', req.blocks.feature_rows(st['tokens'], st['positions'], self.image_id))
         # readout rows of this step and the last layer's tables for them: each row attends to its segment's path up
         # to and including itself (reference `lean_core.py:713-727`)
         rows = sorted({r for kk, r in plan['readout'] if kk == k})
@@ -640,98 +684,102 @@ class LeanGemma4:
                 k_pool.shape[0], out.data_ptr(), t.ptr(qo), t.ptr(kv_indptr), t.ptr(kv_indices), None, n_seg, n_bidir,
                 self.hq, hk, d, 1, window, 1.0, t.ptr(work), n_work, self._stream())
 
-    def _step(self, k, st, plan, pools, head, req, tables):
-        """One forward over a planned step (reference `lean_core.py:599-694`); returns (the residual rows of the
-        step's readout tokens after the last layer, their row indices in the step)."""
+    def _step(self, k, st, plan, pools, head, req, tables, out):
+        """One forward over a planned step (`lean_core.py:599-694`): embedding and first norm, every full layer, the
+        pruned last layer; the residual rows of the step's readout tokens go to `out` (rows in step-row order)."""
         t, rows, n_work = tables
-        s = self._stream()
         n = len(st['tokens'])
-        H, eps, hq = self.hidden, self.eps, self.hq
+        H, hq = self.hidden, self.hq
         dev, bf = self.device, torch.bfloat16
-        nb = int(st['n_bidir'])
-        n_seg = len(st['qo_indptr']) - 1
         if self.peer is not None:
             x, h = self._peer_rows(n)
         else:
             x = torch.empty(n, H, dtype=bf, device=dev)
             h = torch.empty(n, H, dtype=bf, device=dev)
-        max_pos = int(np.max(st['positions'])) if n else 0
         for kind in set(self.types):
-            self._rope(kind, max_pos)
+            self._rope(kind, int(np.max(st['positions'])) if n else 0)
         feat = req.features
         self._k('rows', 'morj_embed_rmsnorm', t.ptr('tokens'), t.ptr('feature_row') if feat is not None else None,
-                 _ptr(feat), self.embed.data_ptr(), n, H, self.embed_scale, self.layers[0]['in_ln'].data_ptr(), eps,
-                 x.data_ptr(), h.data_ptr(), s)
-        temp = {}
-        if pools is None:  # one forward: a temporary pool per kind, rewritten by every layer of that kind
-            for kind in set(self.types):
-                temp[kind] = self._pool(kind, plan['cap'][KINDS[kind]])
-        last = len(self.layers) - 1
-        F = self.layers[0]['gu'].shape[0] // 2
+                _ptr(feat), self.embed.data_ptr(), n, H, self.embed_scale, self.layers[0]['in_ln'].data_ptr(),
+                self.eps, x.data_ptr(), h.data_ptr(), self._stream())
         d_max = max(dd for _, dd in self.geom.values())
-        q = torch.empty(n, hq * d_max, dtype=bf, device=dev)
-        attn = torch.empty(n, hq * d_max, dtype=bf, device=dev)
-        o = torch.empty(n, H, dtype=bf, device=dev)
-        act = torch.empty(n, F, dtype=bf, device=dev)
-        for i, layer in enumerate(self.layers):
-            kind = layer['kind']
-            hk, d = self.geom[kind]
-            kk = KINDS[kind]
+        bufs = dict(x=x, h=h, q=torch.empty(n, hq * d_max, dtype=bf, device=dev),
+                    attn=torch.empty(n, hq * d_max, dtype=bf, device=dev), o=torch.empty(n, H, dtype=bf, device=dev),
+                    act=torch.empty(n, self.layers[0]['gu'].shape[0] // 2, dtype=bf, device=dev),
+                    nb=int(st['n_bidir']), n_seg=len(st['qo_indptr']) - 1)
+        # one step without kept pools: one temporary pool per layer kind, rewritten by every layer of that kind
+        temp = {} if pools is not None else {kind: self._kv_pool(kind, plan['cap'][KINDS[kind]])
+                                             for kind in set(self.types)}
+        last = len(self.layers) - 1
+        for i in range(len(self.layers)):
+            kind = self.types[i]
             if pools is not None:
-                k_pool, v_pool = pools[i]
+                kv = pools[i]
             else:
-                k_pool, v_pool = temp[kind]
+                kv = temp[kind]
                 if len(head):
-                    self._fill_head(k_pool, v_pool, plan['slot_of'][kk][head], *self.shared_kv[i])
-            has_v = int(kind == 'sliding_attention')
+                    self._copy_head([kv], plan['slot_of'], head, layers=[i])
             if i == last and self.prune_last:
-                return self._last_layer(t, rows, n_work, layer, h, x, k_pool, v_pool, kind, has_v)
-            q_i = q[:, :hq * d]
-            self._qkv(h, layer, 0, n, hq, hk, has_v, d, kind, t.ptr('positions'), t.ptr('slots_' + kk), q_i,
-                      k_pool, v_pool)
-            a_i = attn[:, :hq * d]
-            self._attention(q_i, k_pool, v_pool, a_i, t, 'qo', 'kv_indptr_' + kk, 'kv_indices_' + kk, n_seg,
-                            nb if kind == 'sliding_attention' else 0, kind, 'work_' + kk, n_work[kk])
-            nxt = self.layers[i + 1]['in_ln'] if i < last else layer['in_ln']
-            if self.peer is not None:
-                # x rows go back to every rank once, after the last full layer (the readout gathers them)
-                final = i == last - 1 if self.prune_last else i == last
-                self._peer_site(a_i, layer['o'], 0, n, layer['post_attn'], None, layer['pre_ff'], 1, 0)
-                self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
-                self._peer_site(act, layer['down'], 1, n, layer['post_ff'], layer['scalar'], nxt, int(i < last),
-                                int(final))
-                continue
-            self._gemm(a_i, layer['o'], o)
-            self._reduce(o)
-            self._k('rows', 'morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_attn'].data_ptr(),
-                     layer['pre_ff'].data_ptr(), n, H, eps, s)
-            self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
-            self._gemm(act, layer['down'], o)
-            self._reduce(o)
-            self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_ff'].data_ptr(),
-                     layer['scalar'].data_ptr(), nxt.data_ptr(), n, H, eps, int(i < last), s)
-        # (no pruning) the readout rows' residual stream
-        if not rows:
-            return None, []
-        xr = torch.empty(len(rows), H, dtype=bf, device=dev)
-        self._k('rows', 'morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), len(rows), H, xr.data_ptr(), H, s)
-        return xr, rows
+                self._last_layer(t, rows, n_work, self.layers[i], h, x, kv, out)
+                return
+            self._layer(i, t, n_work, kv, bufs)
+        if rows:  # (no pruning) the readout rows' residual stream
+            self._k('rows', 'morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), len(rows), H, out.data_ptr(), H,
+                    self._stream())
 
-    def _last_layer(self, t, rows, n_work, layer, h, x, k_pool, v_pool, kind, has_v):
-        """Last layer (reference `lean_core.py:696-737`): K/V of every token, then q, attention, O and MLP for the
-        readout rows only."""
+    def _layer(self, i, t, n_work, kv, bufs):
+        """Full decoder layer i over every token of a step (`lean_core.py:655-689`): QKV with the head epilogue into
+        the pools, tree attention, O, residual + norms, gate/up with GeGLU, down, residual x scalar + the next layer's
+        input norm. `bufs` holds the step's x and h (updated in place) and its scratch activations."""
+        layer, kind = self.layers[i], self.types[i]
+        hk, d = self.geom[kind]
+        kk = KINDS[kind]
+        k_pool, v_pool = kv
+        x, h, o, act = bufs['x'], bufs['h'], bufs['o'], bufs['act']
+        n, H, hq, eps, s = x.shape[0], self.hidden, self.hq, self.eps, self._stream()
+        sliding = kind == 'sliding_attention'
+        q, attn = bufs['q'][:, :hq * d], bufs['attn'][:, :hq * d]
+        self._qkv(h, layer, 0, n, hq, hk, int(sliding), d, kind, t.ptr('positions'), t.ptr('slots_' + kk), q,
+                  k_pool, v_pool)
+        self._attention(q, k_pool, v_pool, attn, t, 'qo', 'kv_indptr_' + kk, 'kv_indices_' + kk, bufs['n_seg'],
+                        bufs['nb'] if sliding else 0, kind, 'work_' + kk, n_work[kk])
+        last = len(self.layers) - 1
+        nxt = self.layers[i + 1]['in_ln'] if i < last else layer['in_ln']
+        if self.peer is not None:
+            # x rows go back to every rank once, after the last full layer (the readout gathers them)
+            final = i == last - 1 if self.prune_last else i == last
+            self._peer_site(attn, layer['o'], 0, n, layer['post_attn'], None, layer['pre_ff'], 1, 0)
+            self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
+            self._peer_site(act, layer['down'], 1, n, layer['post_ff'], layer['scalar'], nxt, int(i < last),
+                            int(final))
+            return
+        self._gemm(attn, layer['o'], o)
+        self._reduce(o)
+        self._k('rows', 'morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_attn'].data_ptr(),
+                layer['pre_ff'].data_ptr(), n, H, eps, s)
+        self._gemm(h, layer['gu'], act, nat.EPI_GEGLU)
+        self._gemm(act, layer['down'], o)
+        self._reduce(o)
+        self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), layer['post_ff'].data_ptr(),
+                layer['scalar'].data_ptr(), nxt.data_ptr(), n, H, eps, int(i < last), s)
+
+    def _last_layer(self, t, rows, n_work, layer, h, x, kv, xr):
+        """Last layer (`lean_core.py:696-737`): K/V of every token (later readouts attend to them), then q,
+        attention, O and MLP for the readout rows only; their residual rows end in `xr`."""
         s = self._stream()
         n = h.shape[0]
         H, eps, hq = self.hidden, self.eps, self.hq
+        kind = self.types[-1]
         hk, d = self.geom[kind]
         kk = KINDS[kind]
+        k_pool, v_pool = kv
+        has_v = int(kind == 'sliding_attention')
         dev, bf = self.device, torch.bfloat16
         qd = hq * d
-        # K/V of every token (later readouts attend to them), straight into the pools
         self._qkv(h, layer, qd, n, 0, hk, has_v, d, kind, t.ptr('positions'), t.ptr('slots_' + kk), None, k_pool,
                   v_pool)
         if not rows:
-            return None, []
+            return
         R = len(rows)
         hr = torch.empty(R, H, dtype=bf, device=dev)
         self._k('rows', 'morj_gather_rows', h.data_ptr(), H, t.ptr('ro_rows'), R, H, hr.data_ptr(), H, s)
@@ -743,19 +791,16 @@ class LeanGemma4:
         o = torch.empty(R, H, dtype=bf, device=dev)
         self._gemm(attn, layer['o'], o)
         self._reduce(o)
-        xr = torch.empty(R, H, dtype=bf, device=dev)
         self._k('rows', 'morj_gather_rows', x.data_ptr(), H, t.ptr('ro_rows'), R, H, xr.data_ptr(), H, s)
         h2 = torch.empty(R, H, dtype=bf, device=dev)
         self._k('rows', 'morj_attn_epilogue', o.data_ptr(), xr.data_ptr(), h2.data_ptr(), layer['post_attn'].data_ptr(),
-                 layer['pre_ff'].data_ptr(), R, H, eps, s)
-        F = layer['gu'].shape[0] // 2
-        act = torch.empty(R, F, dtype=bf, device=dev)
+                layer['pre_ff'].data_ptr(), R, H, eps, s)
+        act = torch.empty(R, layer['gu'].shape[0] // 2, dtype=bf, device=dev)
         self._gemm(h2, layer['gu'], act, nat.EPI_GEGLU)
         self._gemm(act, layer['down'], o)
         self._reduce(o)
         self._k('rows', 'morj_mlp_epilogue', o.data_ptr(), xr.data_ptr(), xr.data_ptr(), layer['post_ff'].data_ptr(),
-                 layer['scalar'].data_ptr(), layer['in_ln'].data_ptr(), R, H, eps, 0, s)
-        return xr, rows
+                layer['scalar'].data_ptr(), layer['in_ln'].data_ptr(), R, H, eps, 0, s)
 
     def forward_tree(self, tree, label_ids):
         """Every sequence of an already built tree in one pass (reference `lean_core.py:739-742`)."""

@@ -112,6 +112,47 @@ def gather_handles(group, handle):
     return out
 
 
+class PassProtocol:
+    """Host-side agreement of a tensor-parallel group around every pass over peer memory.
+
+    The exchange kernels wait on counters that other ranks advance, and give up after a bounded time (device codes
+    0x104 / 0x105). Two host rules keep that bound from firing, or from leaving the group out of step, when the ranks'
+    hosts do not start a pass together (planning a larger tree, a request arriving on one rank later, a pause):
+      * `begin()` before a pass launches anything: a barrier over the group, so no rank's kernels start waiting on
+        a peer whose host has not reached the pass yet;
+      * `agree(code)` after the pass: the largest device error code over the group, so every rank sees a failure any
+        rank saw, and `recover(clear)` then runs on all of them: wait for the GPU, barrier, zero the counters
+        (`clear`), barrier. The next pass then starts every counter from zero again (the host's cumulative targets
+        restart with `sites` = 0)."""
+
+    def __init__(self, group, device=None):
+        import torch.distributed as dist
+        self.group = group
+        self.device = device if dist.get_backend(group) == 'nccl' else None
+
+    def begin(self):
+        import torch.distributed as dist
+        dist.barrier(group=self.group)
+
+    def agree(self, code):
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([int(code)], dtype=torch.int64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return int(t.item())
+
+    def recover(self, clear):
+        import torch
+        import torch.distributed as dist
+        if self.device is not None:
+            torch.cuda.synchronize(self.device)  # every wait still running ends by its own bound
+        dist.barrier(group=self.group)
+        clear()
+        if self.device is not None:
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+
 class PeerExchange:
     """This rank's exchange buffers, mapped into every peer (CUDA IPC), and the `morj_peer_t` that describes them.
 
@@ -150,7 +191,26 @@ class PeerExchange:
         self.desc = d
         self.regions = lay['regions']
         self.sites = 0
+        self.protocol = PassProtocol(group, device)
         dist.barrier(group=group)
+
+    def begin_pass(self):
+        """Before a pass launches anything (see `PassProtocol.begin`)."""
+        self.protocol.begin()
+
+    def end_pass(self, code):
+        """After a pass: the group's largest device error code; on a failure anywhere, every rank zeroes its counters
+        and restarts the site count (see `PassProtocol`)."""
+        code = self.protocol.agree(code)
+        if code:
+            self.protocol.recover(self._clear_counters)
+        return code
+
+    def _clear_counters(self):
+        for name in ('partials', 'rows'):
+            off, size = self.regions[name]
+            self.buf[off:off + size].zero_()
+        self.sites = 0
 
     def rows_view(self, name, n):
         """This rank's x or h rows [n, hidden] (BF16) inside the exchange allocation."""

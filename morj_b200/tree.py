@@ -93,45 +93,42 @@ class Tree:
         return self.nodes[nid][2] - self.nodes[nid][1]
 
     def readout_slot(self, b):
-        """(node, tree offset) of sequence `b`'s last token (reference `lean_core.py:88-94`)."""
-        last = len(self.seqs[b]) - 1
-        for nid in self.paths[b]:
-            _, s, e = self.nodes[nid]
-            if s <= last < e:
-                return nid, int(self.offsets[nid] + last - s)
-        raise ValueError('empty sequence')
+        """(node, tree offset) of sequence `b`'s last token, the row its label distribution is read from
+        (`lean_core.py:88-94`). A sequence's path covers its depths [0, len) in order, so the token is the last one
+        of the path's last node."""
+        path = self.paths[b]
+        if not len(self.seqs[b]) or not path:
+            raise ValueError('empty sequence')
+        nid = path[-1]
+        return nid, int(self.offsets[nid] + len(self.seqs[b]) - 1 - self.nodes[nid][1])
 
     def pass_nodes(self, seqs, cached):
-        """Nodes a pass over `seqs` computes: uncached path nodes plus every readout node, whose hidden state is not
-        kept and is computed again (reference `lean_core.py:96-101`)."""
-        need = set()
-        for b in seqs:
-            need.update(self.paths[b])
-        need.difference_update(cached)
-        for b in seqs:
-            need.add(self.readout_slot(b)[0])
-        return sorted(need)
+        """Node ids (sorted) a pass over sequences `seqs` computes when the nodes `cached` already have their K/V: the
+        rest of their paths, and always their readout nodes, whose hidden states are never kept
+        (`lean_core.py:96-101`)."""
+        on_paths = np.unique(np.fromiter((n for b in seqs for n in self.paths[b]), dtype=np.int64))
+        fresh = np.setdiff1d(on_paths, np.fromiter(cached, dtype=np.int64, count=len(cached)))
+        readout = np.fromiter((self.paths[b][-1] for b in seqs), dtype=np.int64, count=len(seqs))
+        return np.union1d(fresh, readout).astype(int).tolist()
 
     def pinned_for(self, done, future, window):
-        """Offsets a later pass over `future` reads once this pass has computed `done`: per future path, every token
-        before its first node that is not done (or its readout node, always recomputed); all of them for full layers
-        ('g'), the last `window` before that point for sliding layers ('s') (reference `lean_core.py:103-118`)."""
-        keep = {'g': [], 's': []}
+        """Tree offsets that later passes over sequences `future` read from this pass's K/V, once the nodes `done`
+        are computed (`lean_core.py:103-118`). Along each future path, the K/V a later pass reads are those of the
+        tokens before its first node it must compute: the first node not done, or at the latest the readout node
+        (the path's last, always computed again). Full-attention layers ('g') keep all of them; sliding layers ('s')
+        only the `window - 1` nearest, the rest is out of every later query's window."""
+        keep_g, keep_s = [], []
         for f in future:
             path = self.paths[f]
-            ro = self.readout_slot(f)[0]
-            j = len(path)
-            for i, n in enumerate(path):
-                if n not in done or n == ro:
-                    j = i
-                    break
+            j = next((i for i, n in enumerate(path[:-1]) if n not in done), len(path) - 1)
             if j == 0:
                 continue
             before = np.concatenate([self.slots(n) for n in path[:j]])
-            d0 = self.nodes[path[j]][1] if j < len(path) else self.nodes[path[-1]][2]
-            keep['g'].append(before)
-            keep['s'].append(before[max(0, d0 - window + 1):])
-        return {k: (np.unique(np.concatenate(v)) if v else np.zeros(0, np.int64)) for k, v in keep.items()}
+            keep_g.append(before)
+            keep_s.append(before[max(0, len(before) - (window - 1)):])
+        empty = np.zeros(0, np.int64)
+        return {'g': np.unique(np.concatenate(keep_g)) if keep_g else empty,
+                's': np.unique(np.concatenate(keep_s)) if keep_s else empty}
 
     # ---- planning -------------------------------------------------------------------------------------------------
     def plan_pass(self, compute, readout_seqs, window, single_max, step_tokens, identity, prealloc=(), initial=None,

@@ -321,17 +321,17 @@ class OracleModel:
     def forward_tree(self, tree_cls, seqs, label_ids, precision='bf16', single_max=16384, step_tokens=8192,
                      images=None, expand=None):
         """Plan one pass over every sequence with `tree_cls` (a planner bit-exact with the reference's) and run it;
-        returns per-sequence label probabilities. `expand`: the engine's image expansion helper when images are
-        given (placeholder expansion and block splits, reference `lean_core.py:433-462`)."""
+        returns per-sequence label probabilities. `expand`: the engine's image layout (`ImageBlocks`: placeholder
+        expansion, block bounds and splits, reference `lean_core.py:433-462`) when images are given."""
         bf16 = precision == 'bf16'
         splits, layout, feats = [], None, None
         seqs = [list(s) for s in seqs]
         if images:
             layout = expand(seqs, images, self.image_id, self.top['boi_token_id'], self.top['eoi_token_id'])
-            seqs, splits = layout['seqs'], layout['splits']
+            seqs, splits = layout.seqs, layout.splits
             feats = torch.cat([f.float() for f in images])
         tree = tree_cls(seqs + splits)
-        bidir = layout['bidir_nodes'](tree) if layout else frozenset()
+        bidir = layout.bidir_nodes(tree) if layout else frozenset()
         idx = list(range(len(seqs)))
         need = tree.pass_nodes(idx, set())
         plan = tree.plan_pass(need, idx, self.window, single_max, step_tokens, False, bidir=bidir)
@@ -344,8 +344,8 @@ class OracleModel:
                 fr = np.full(len(st['tokens']), -1)
                 im = np.flatnonzero(st['tokens'] == self.image_id)
                 depth = st['positions'][im]
-                kb = np.searchsorted(layout['blob_start'], depth, side='right') - 1
-                fr[im] = layout['blob_off'][kb] + depth - layout['blob_start'][kb]
+                kb = np.searchsorted(layout.start, depth, side='right') - 1
+                fr[im] = layout.off[kb] + depth - layout.start[kb]
             finals.append(self.forward_step(st, plan['cap'], rows, pools if len(plan['steps']) > 1 else None, fr,
                                             feats, precision))
         rows = [finals[k][r] for k, r in plan['readout']]

@@ -87,3 +87,54 @@ def test_handles_are_swapped_in_rank_order_over_gloo():
     mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True, start_method='spawn')
     for r in range(world):
         assert out[r] == [bytes([q]) * 72 for q in range(world)]
+
+
+def _protocol_rank(rank, world, port, out):
+    """One rank of a pass sequence in which rank 1 reaches pass 1 three seconds late and reports a device error
+    (0x104, a peer wait that ran out) in pass 2."""
+    import time
+
+    import torch
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        from morj_b200.tp import PassProtocol
+        proto = PassProtocol(dist.group.WORLD)
+        counters = torch.full((4,), 7, dtype=torch.int64)  # stand-in for the rank's counter regions
+        sites = [5]
+
+        def clear():
+            counters.zero_()
+            sites[0] = 0
+        log = []
+        for pas in (1, 2, 3):
+            if pas == 1 and rank == 1:
+                time.sleep(3.0)
+            t0 = time.time()
+            proto.begin()
+            log.append(('begin', pas, t0, time.time()))
+            code = proto.agree(0x104 if (pas == 2 and rank == 1) else 0)
+            if code:
+                proto.recover(clear)
+            log.append(('end', pas, code, int(counters.sum()), sites[0]))
+        out[rank] = log
+    finally:
+        dist.destroy_process_group()
+
+
+def test_pass_protocol_holds_an_early_rank_and_shares_a_failure_over_gloo():
+    """A rank that reaches a pass late holds the others at the pass barrier (so no kernel waits on it against its
+    bound), and a device failure on one rank is seen by all, which all zero their counters and go on in step."""
+    world = 2
+    out = mp.Manager().dict()
+    mp.start_processes(_protocol_rank, args=(world, _free_port(), out), nprocs=world, join=True, start_method='spawn')
+    r0, r1 = out[0], out[1]
+    begin0 = [e for e in r0 if e[0] == 'begin' and e[1] == 1][0]
+    begin1 = [e for e in r1 if e[0] == 'begin' and e[1] == 1][0]
+    assert begin0[3] >= begin1[2] - 0.05  # rank 0 left the first barrier only once the late rank reached it
+    assert begin0[3] - begin0[2] > 2.0
+    for log in (r0, r1):
+        ends = {e[1]: e for e in log if e[0] == 'end'}
+        assert ends[1][2] == 0 and ends[3][2] == 0
+        assert ends[2][2] == 0x104  # both ranks see rank 1's failure
+        assert ends[2][3] == 0 and ends[2][4] == 0  # and both cleared their counters and the site count

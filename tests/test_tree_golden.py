@@ -54,12 +54,12 @@ def test_multimodal_trees_match_reference_prepare_and_plan(idx):
     cfg = w.gemma31b_config()
     t = w.multimodal_tree(0, **case['kw'])
     layout = expand_images(t['seqs'], t['images'], cfg['image_token_id'], cfg['boi_token_id'], cfg['eoi_token_id'])
-    tree = Tree(layout['seqs'] + layout['splits'])
+    tree = Tree(layout.seqs + layout.splits)
     assert [list(map(int, s)) for s in tree.seqs] == case['expanded']
-    bidir = layout['bidir_nodes'](tree)
+    bidir = layout.bidir_nodes(tree)
     assert sorted(bidir) == case['bidir']
-    assert layout['blob_start'].tolist() == case['blob_start'] and layout['blob_end'].tolist() == case['blob_end']
-    assert layout['blob_off'].tolist() == case['blob_off']
+    assert layout.start.tolist() == case['blob_start'] and layout.end.tolist() == case['blob_end']
+    assert layout.off.tolist() == case['blob_off']
     assert tree_record(tree) == case['tree']
     seqs = list(range(case['n_real']))
     need = tree.pass_nodes(seqs, set())

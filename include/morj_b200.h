@@ -232,8 +232,9 @@ int morj_peer_wait(const morj_peer_t* peer, int n, unsigned long long row_target
  * the block counters) is a fixed array inside the library, 8 MiB plus 16 KiB, held by every GPU that loads the
  * library until exit: M * N * 2 must not exceed 8 MiB (and M must not exceed 131072), larger calls are rejected
  * with MORJ_ERR_ARG. The first call on a device looks the array's address up (cudaGetSymbolAddress); make that
- * first call before any stream capture. Every call shares the array: calls that overlap on the GPU race and must be
- * ordered by the caller. Allocates nothing. */
+ * first call before any stream capture. The address is cached per device number for the process's life: after
+ * cudaDeviceReset do not call it again in that process. h may be NULL for mode 1 with has_next = 0. Every call
+ * shares the array: calls that overlap on the GPU race and must be ordered by the caller. Allocates nothing. */
 int morj_gemm_norm_epilogue_noalloc(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                                     int mode, void* x, void* h, const void* w_a, const void* scalar, const void* w_b,
                                     float eps, int has_next, void* stream);

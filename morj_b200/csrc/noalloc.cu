@@ -25,7 +25,9 @@ constexpr size_t kScratchBytes = kPartBytes + 2 * kMaxBlocks * sizeof(unsigned l
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 // The device address of g_scratch on the current device. In host code `g_scratch` names a host-side stand-in, not
-// device memory, so the address is looked up once per device (with that device current) and cached.
+// device memory, so the address is looked up once per device (with that device current) and cached for the life of
+// the process. The cache is keyed by device number: after cudaDeviceReset (or from a second context on the same
+// device) the cached address is stale, so a process that resets a device must not call this entry point again.
 static int scratch_address(unsigned char** out) {
   constexpr int kMaxDevices = 64;
   static unsigned char* addr[kMaxDevices] = {};
@@ -58,11 +60,16 @@ extern "C" int morj_gemm_norm_epilogue_noalloc(const void* A, long long lda, con
     return set_error(MORJ_ERR_ARG, "morj_gemm_norm_epilogue_noalloc: bad arguments (M=%d N=%d K=%d mode=%d)", M, N,
                      K, mode);
   const long long blocks = (M + 127) / 128;
-  if ((unsigned long long)M * (unsigned long long)N * 2 > noalloc::kPartBytes || blocks > noalloc::kMaxBlocks)
+  if ((unsigned long long)M * (unsigned long long)N * 2 > noalloc::kPartBytes)
     return set_error(MORJ_ERR_ARG,
-                     "morj_gemm_norm_epilogue_noalloc: M x N = %d x %d needs %lld bytes of scratch, above the "
-                     "library's fixed %zu",
+                     "morj_gemm_norm_epilogue_noalloc: M x N = %d x %d needs %lld bytes of projection scratch, above "
+                     "the library's fixed %zu",
                      M, N, (long long)M * N * 2, noalloc::kPartBytes);
+  if (blocks > noalloc::kMaxBlocks)
+    return set_error(MORJ_ERR_ARG,
+                     "morj_gemm_norm_epilogue_noalloc: M = %d rows need %lld row blocks of 128, above the library's "
+                     "fixed %d counter pairs (M <= %d)",
+                     M, blocks, noalloc::kMaxBlocks, noalloc::kMaxBlocks * 128);
   unsigned char* scratch = nullptr;
   int st = noalloc::scratch_address(&scratch);
   if (st) return st;

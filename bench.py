@@ -9,9 +9,13 @@ probabilities (planning, host-to-device tables, kernels, device-to-host probabil
 N > 1: one process per GPU, each a full model replica on its own seeded tree (independent trees: no collective on
 the data path; weak scaling). Weights (~52 GB BF16) and every input are larger than L2, so no L2 flush is needed.
 
-`--impl reference` times the reference lean path on the host CPU (its restatement in `oracle/lean_oracle.py`: the
-reference has no CPU implementation of its GPU path) on the same workload: one sliding and one global decoder layer
-at the full token count, extrapolated to the 60-layer pattern.
+`e2e` calls `prepare` then `run` per request, as `LeanEngine._score_pass` does (`lean_engine.py:111-122`).
+
+`--impl reference` times the reference's own lean path (`aleria_judge/lean_core.py`, unmodified, installed under
+`baseline/_ref`) on the host CPU, on the same workload tree: `LeanGemma4.prepare` + `run` over a 3-layer cut of the
+model (one sliding, one global and the pruned global last layer) with torch-eager stand-ins for its GPU-only
+FlashInfer calls and Triton kernels (`oracle/ref_cpu.py`). `ms_per_step` is that timed step; `value` extrapolates its
+per-layer times to the 60-layer pattern. This process never loads the B200 library (`native_library_loaded`).
 """
 import argparse
 import json
@@ -95,69 +99,6 @@ class Clocks:
                 'reasons': reasons, 'samples': len(self.rows), 'power_w_max': max(power) if power else None}
 
 
-class CpuLayers:
-    """The reference lean path's per-layer work on the host CPU (the oracle in BF16, torch on every host thread):
-    one sliding and one global decoder layer of the 31B-class model at the text tree's full token count. A tree costs
-    50 sliding + 10 global layers; embedding and readout are < 0.01% of the FLOPs and left out."""
-
-    def __init__(self):
-        import torch
-        from morj_b200 import workloads as w
-        from morj_b200.checkpoint import tensor_shapes
-        from morj_b200.tree import Tree
-        from oracle.lean_oracle import OracleModel, rope_tables
-        torch.set_num_threads(os.cpu_count())
-        top = w.gemma31b_config()
-        cfg = dict(top['text_config'])
-        self.layer_types = list(cfg['layer_types'])
-        cfg['layer_types'] = ['sliding_attention', 'full_attention']
-        cfg['num_hidden_layers'] = 2
-        small = dict(top, text_config=dict(cfg, vocab_size=16))
-        # timing only: weights are a tiled seeded random block (their values do not change the work)
-        block = (torch.randn(1 << 22, generator=torch.Generator().manual_seed(0)) * 0.02).to(torch.bfloat16)
-        state = {}
-        for k, shape in tensor_shapes(small):
-            n = int(np.prod(shape))
-            if len(shape) == 1:
-                state[k] = torch.ones(shape, dtype=torch.bfloat16)
-            else:
-                state[k] = block.repeat(-(-n // block.numel()))[:n].reshape(shape).clone()
-        self.model = OracleModel(small, state)
-        tree_in = w.text_tree(0)
-        tree = Tree(tree_in['seqs'])
-        need = tree.pass_nodes(range(len(tree.seqs)), set())
-        self.plan = tree.plan_pass(need, list(range(len(tree.seqs))), cfg['sliding_window'], 16384, 8192, False)
-        self.st = self.plan['steps'][0]
-        self.tokens = len(self.st['tokens'])
-        g = torch.Generator().manual_seed(1)
-        self.x = torch.randn(self.tokens, cfg['hidden_size'], generator=g).to(torch.bfloat16).float()
-        self.rope = {k: rope_tables(self.st['positions'], v) for k, v in self.model.inv.items()}
-
-    def layer_seconds(self, i):
-        t0 = time.perf_counter()
-        self.model.layer(i, self.x, self.x, self.st, self.plan['cap'], self.rope, None, 'bf16')
-        return time.perf_counter() - t0
-
-    def tree_seconds(self):
-        """One sample: time a sliding and a global layer, extrapolate to the 60-layer pattern."""
-        t_s, t_g = self.layer_seconds(0), self.layer_seconds(1)
-        sl = sum(1 for k in self.layer_types if k == 'sliding_attention')
-        return sl * t_s + (len(self.layer_types) - sl) * t_g, t_s, t_g
-
-
-def cpu_layer_baseline(budget_s=30.0):
-    layers = CpuLayers()
-    layers.tree_seconds()  # warm-up
-    first = layers.tree_seconds()
-    samples = [first]
-    if first[1] + first[2] < budget_s / 3:
-        samples += [layers.tree_seconds() for _ in range(2)]
-    per_tree = statistics.median(s[0] for s in samples)
-    return dict(tokens=layers.tokens, seconds_per_tree=per_tree, sliding_s=statistics.median(s[1] for s in samples),
-                global_s=statistics.median(s[2] for s in samples), runs=len(samples), cores=os.cpu_count(),
-                cpu=_cpu_model())
-
-
 def _cpu_model():
     try:
         with open('/proc/cpuinfo') as f:
@@ -169,29 +110,102 @@ def _cpu_model():
     return 'unknown'
 
 
+def _native_loaded():
+    """Whether this process has mapped the B200 library (the reference arm must not)."""
+    try:
+        with open('/proc/self/maps') as f:
+            return any('_morj_b200' in line for line in f)
+    except OSError:
+        return None
+
+
+def tree_flops(top, plan, tokens):
+    """Algorithmic FLOPs of one pass: 2 x linear parameters per computed token plus 4 x Hq x d per visible (query,
+    key) pair, from a planner's pass plan (the reference's and this engine's plans are identical)."""
+    from morj_b200 import workloads as w
+    c = top['text_config']
+    pairs = w.attention_pairs(plan, c['sliding_window'], c['layer_types'])
+    return w.linear_flops_per_token(top) * tokens + 4 * c['num_attention_heads'] * c['head_dim'] * pairs
+
+
+def bench_config(args, world, desc, tokens, flops):
+    """The `config` object of the JSON line; both arms print the same one for the same arguments."""
+    tp = args.mode == 'tp' and world > 1
+    par = (f'replicas x{world} (independent trees, no collective)' if not tp else
+           f'tensor parallel x{world} (O/down partial rows read by their row owners over NVLink, reduced with the '
+           f'epilogues)' if args.tp_comm == 'peer' else f'tensor parallel x{world} (NCCL all-reduce after O and down)')
+    work = (f'31B-class Gemma-style decoder, {desc}' if not args.layers else
+            f'31B-class Gemma-style decoder cut to {args.layers} layers (profiling), {desc}')
+    return dict(workload=work, tokens=tokens, parallelism=par,
+                l2='inputs larger than L2 (52 GB of weights streamed per step)',
+                tflops_per_tree_specified=round(flops / 1e12, 2))
+
+
+def reference_cpu(args, rank=0):
+    """The reference's own lean path on the host CPU (`oracle.ref_cpu.TimedReference`) over this run's workload
+    tree; raises ImportError when the reference package is not installed beside the repository."""
+    import torch
+    from morj_b200 import workloads as w
+    from oracle.ref_cpu import TimedReference
+    torch.set_num_threads(os.cpu_count())
+    top = w.gemma31b_config()
+    if args.layers:
+        top = w.reduced_config(top, args.layers)
+    tree_in, desc = workload(args.workload, rank)
+    if isinstance(tree_in, list):
+        raise ImportError('the CPU reference times one request tree, not a forest sweep')
+    return TimedReference(top, tree_in), top, desc
+
+
+def cpu_reference_line(tr, samples):
+    med = {k: statistics.median(s[k] for s in samples) for k in ('seconds', 'setup', 'sliding', 'global_', 'last')}
+    tree_s = statistics.median(tr.extrapolate(s) for s in samples)
+    body = tr.full_types[:-1]
+    n_s = sum(1 for k in body if k == 'sliding_attention')
+    return tree_s, samples[0]['tokens'], dict(
+        step=('the reference LeanGemma4.prepare + run (aleria_judge/lean_core.py:428-576, unmodified, from '
+              'baseline/_ref) on the host CPU over a 3-layer cut of the model (1 sliding, 1 global, the pruned global '
+              'last layer) at the full tree; FlashInfer and its 3 Triton kernels replaced by torch-eager stand-ins '
+              '(oracle/ref_cpu.py)'),
+        ms_per_step_timed=round(1000 * med['seconds'], 1),
+        ms_setup=round(1000 * med['setup'], 1), ms_sliding_layer=round(1000 * med['sliding'], 1),
+        ms_global_layer=round(1000 * med['global_'], 1), ms_last_layer_and_readout=round(1000 * med['last'], 1),
+        extrapolated_tree_ms=round(1000 * tree_s, 1),
+        extrapolation=f'setup + {n_s} x sliding + {len(body) - n_s} x global + last',
+        samples=len(samples), cores=os.cpu_count(), threads=__import__('torch').get_num_threads(), cpu=_cpu_model())
+
+
 def reference_arm(args, rank, world):
-    """The reference arm: rank 0 times the CPU restatement of the reference lean path (no other rank works)."""
+    """The reference arm: rank 0 times the reference's own lean path on the host CPU (no other rank works). A step is
+    one request through a 3-layer cut of the model; `ms_per_step` is that timed step, `value` the tokens/s of the
+    whole model extrapolated from its per-layer times (the metric is per 60-layer tree)."""
     if rank != 0:
         return
-    layers = CpuLayers()
-    steps = []
-    for i in range(args.warmup + args.steps):
-        per_tree, t_s, t_g = layers.tree_seconds()
-        if i >= args.warmup:
-            steps.append(dict(tokens=layers.tokens, seconds_per_tree=per_tree, cores=os.cpu_count(),
-                              cpu=_cpu_model()))
-    r = steps[-1]
-    value = r['tokens'] * len(steps) / sum(x['seconds_per_tree'] for x in steps)
+    try:
+        tr, top, desc = reference_cpu(args)
+    except ImportError as error:
+        print(json.dumps(dict(impl='reference', unavailable=f'reference package not installed: {error}')),
+              flush=True)
+        return
+    for _ in range(args.warmup):
+        tr.sample()
+    samples = [tr.sample() for _ in range(args.steps)]
+    tree_s, tokens, run = cpu_reference_line(tr, samples)
+    plan = tr.plan_of_last_request()
+    value = tokens / tree_s
     line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=1000 * r['seconds_per_tree'], higher_is_better=True, scaling='weak', vs_baseline=None,
-                dtype='bf16', data='synthetic', impl='reference',
-                config=dict(workload='31B-class text tree (1500 + 9 x 60 tokens), CPU, layer-extrapolated',
-                            tokens=r['tokens'], l2='inputs larger than L2'),
-                cpu_baseline=dict(value=value, unit=UNIT, cores=r['cores'], kind='port',
-                                  sample=('one sliding + one global decoder layer at the full 2040-token tree '
-                                          'through oracle/lean_oracle.py (BF16, torch CPU), extrapolated x50 + x10'),
-                                  cpu=r['cpu']),
-                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+                ms_per_step=run['ms_per_step_timed'], higher_is_better=True,
+                scaling='strong' if args.mode == 'tp' and world > 1 else 'weak', vs_baseline=None,
+                dtype='bf16', data='synthetic (timing weights: a seeded N(0, 0.02) block tiled; uniform token ids)',
+                impl='reference', value_basis='extrapolated from the timed 3-layer step to the full layer pattern',
+                config=bench_config(args, world, desc, tokens, tree_flops(top, plan, tokens)),
+                reference_run=run,
+                cpu_baseline=dict(value=value, unit=UNIT, cores=os.cpu_count(), kind='reference',
+                                  sample=(f'{args.steps} requests of the {tokens}-token tree through the reference '
+                                          f'run on a 3-layer cut, extrapolated to {len(tr.full_types)} layers'),
+                                  cpu=_cpu_model()),
+                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+                native_library_loaded=_native_loaded())
     print(json.dumps(line), flush=True)
 
 
@@ -355,15 +369,16 @@ def main():
     init_s = time.perf_counter() - t_init
     tree_in, desc = workload(args.workload, 0 if tp else rank)
     requests = tree_in if isinstance(tree_in, list) else [tree_in]
-    reqs, preps = [], []
+    for r in requests:  # image features start in pinned host memory (the end-to-end call copies them in)
+        r['host_images'] = [f.pin_memory() for f in r['images']] if r['images'] else None
+    preps = []
     for r in requests:
         images = [f.to(dev) for f in r['images']] if r['images'] else None
         req = model.prepare(r['seqs'], r['label_ids'], images=images)
-        reqs.append((req, list(range(len(r['seqs'])))))
         preps.append(model.prepare_pass(req, list(range(len(r['seqs'])))))
     tokens = sum(p['tokens'] for p in preps)
     c = top['text_config']
-    flops_lin = w.linear_flops_per_token(top) * tokens
+    flops = sum(tree_flops(top, p['plan'], p['tokens']) for p in preps)
     pairs = sum(w.attention_pairs(p['plan'], c['sliding_window'], c['layer_types']) for p in preps)
     flops_attn = 4 * c['num_attention_heads'] * c['head_dim'] * pairs
 
@@ -371,9 +386,19 @@ def main():
         for p in preps:
             model.execute_pass(p)
 
+    copied = {'h2d': 0, 'd2h': 0}
+
     def run_all():
-        for req, seqs in reqs:
-            model.run(req, seqs)
+        """What a caller does per request (`LeanEngine._score_pass`, `lean_engine.py:111-122`): prepare, then run;
+        host token ids and pinned host image features in, host probabilities out."""
+        out, h2d, d2h = [], 0, 0
+        for r in requests:
+            req = model.prepare(r['seqs'], r['label_ids'], images=r['host_images'])
+            out.append(model.run(req, list(range(len(r['seqs'])))))
+            h2d += model.h2d_bytes + sum(f.numel() * f.element_size() for f in r['host_images'] or [])
+            d2h += model.d2h_bytes
+        copied.update(h2d=h2d, d2h=d2h)
+        return out
     props = torch.cuda.get_device_properties(dev)
     clocks = Clocks('GPU-' + str(props.uuid) if hasattr(props, 'uuid') else str(local))
 
@@ -393,9 +418,9 @@ def main():
         barrier()
         ms = e0.elapsed_time(e1) / args.steps
         launches = (model.launches - launches0) // args.steps
-        # ---- end to end through the public call (host ids -> host probabilities) --------------------------------
+        # ---- end to end through the public calls (host ids -> host probabilities) -------------------------------
         for _ in range(2):
-            run_all()
+            probs = run_all()
         barrier()
         lat = []
         e2 = torch.cuda.Event(enable_timing=True)
@@ -409,8 +434,7 @@ def main():
         barrier()
         clocks.stop()
         e2e_ms = e2.elapsed_time(e3) / args.steps
-        h2d = sum(p['h2d_bytes'] for p in preps) if len(preps) > 1 else model.h2d_bytes
-        d2h = 4 * sum(p['ro']['n_labels'] for p in preps)
+        h2d, d2h = copied['h2d'], copied['d2h']
         # ---- the same planned pass captured once in a CUDA graph and replayed (launch gaps between kernels gone) ----
         graph_ms = None
         if not tp:  # (a graph holding NCCL calls is not worth its teardown rules here)
@@ -461,39 +485,61 @@ def main():
         kname = tr.get('kernel', kname)
         if tr.get('M') == tokens and not tp and len(preps) == 1:
             traffic = tr.get('bytes_per_launch')
+    attn_ms = per_kind.get('attention', {}).get('ms', 0.0)
+    parity = None
+    if rank == 0 and args.workload == 'text' and not args.layers:
+        # the bench tree's probabilities against the oracle's on the same weights and tree, recorded by
+        # tests/golden/make_oracle_31b.py (tests/test_gpu_parity_31b.py checks the record reproduces)
+        gfile = os.path.join(ROOT, 'tests', 'golden', 'oracle_31b_text.json')
+        if os.path.exists(gfile):
+            with open(gfile) as f:
+                rec = json.load(f)
+            got = np.concatenate([np.asarray(r, np.float64) for r in probs[0]])
+            bf = np.concatenate([np.asarray(r, np.float64) for r in rec['probs']])
+            fp = np.concatenate([np.asarray(r, np.float64) for r in rec['probs_fp32']])
+            parity = dict(vs='oracle on the same weights and tree: BF16 (the reference lean path\'s rounding points) '
+                             'and FP32 (the exact model)',
+                          max_abs_vs_bf16_path=float(np.abs(got - bf).max()),
+                          max_abs_vs_fp32=float(np.abs(got - fp).max()),
+                          bf16_path_max_abs_vs_fp32=float(np.abs(bf - fp).max()), probabilities=int(len(got)))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            r = cpu_layer_baseline()
-            cpu = dict(value=r['tokens'] / r['seconds_per_tree'], unit=UNIT, cores=r['cores'], kind='port',
-                       sample=(f"one sliding ({r['sliding_s']:.2f} s) + one global ({r['global_s']:.2f} s) decoder "
-                               f"layer at the full {r['tokens']}-token tree through oracle/lean_oracle.py (BF16, torch "
-                               f"CPU, median of {r['runs']}), extrapolated x50 + x10"), cpu=r['cpu'])
+            tr, _, _ = reference_cpu(args)
+            tr.sample()  # warm-up
+            samples = [tr.sample() for _ in range(2)]
+            tree_s, ref_tokens, run = cpu_reference_line(tr, samples)
+            cpu = dict(value=ref_tokens / tree_s, unit=UNIT, cores=os.cpu_count(), kind='reference',
+                       sample=(f"2 requests of the {ref_tokens}-token tree through the reference's LeanGemma4.run on "
+                               f"the host CPU over a 3-layer cut (sliding {run['ms_sliding_layer']} ms, global "
+                               f"{run['ms_global_layer']} ms per layer), extrapolated to {len(tr.full_types)} layers"),
+                       cpu=run['cpu'], threads=run['threads'])
+            del tr
         except Exception as error:  # the baseline must not take the GPU number down with it
-            cpu = dict(value=None, unit=UNIT, cores=os.cpu_count(), kind='port', sample=f'failed: {error}')
+            cpu = dict(value=None, unit=UNIT, cores=os.cpu_count(), kind='reference', sample=f'failed: {error}')
     if rank == 0:
         line = dict(
             metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=ms_max, higher_is_better=True, scaling='strong' if tp else 'weak', vs_baseline=None,
             dtype='bf16',
             data='synthetic (seeded random-init weights N(0, 0.02), uniform token ids)',
-            config=dict(workload=(f'31B-class Gemma-style decoder, {desc}' if not args.layers else
-                                  f'31B-class Gemma-style decoder cut to {args.layers} layers (profiling), {desc}'),
-                        tokens=tokens,
-                        parallelism=((f'tensor parallel x{world} (O/down partial rows read by their row owners '
-                                      f'over NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else
-                                      f'tensor parallel x{world} (NCCL all-reduce after O and down)') if tp else
-                                     f'replicas x{world} (independent trees, no collective)'),
-                        l2='inputs larger than L2 (52 GB of weights streamed per step)',
-                        tflops_per_tree_specified=round((flops_lin + flops_attn) / 1e12, 2)),
-            model_tflops=round(trees * (flops_lin + flops_attn) / (ms_max / 1000) / 1e12, 1),
+            config=bench_config(args, world, desc, tokens, flops),
+            model_tflops=round(trees * flops / (ms_max / 1000) / 1e12, 1),
             p50_tree_latency_ms=round(statistics.median(lat), 3),
             roofline=dict(bound='tensor', kernel=f'{kname}: gate/up projection {tokens}x43008x5376',
                           achieved=round(achieved, 1), peak=pk['bf16_sustained'], unit='TFLOP/s',
                           frac=round(achieved / pk['bf16_sustained'], 4), traffic=traffic,
                           peak_source=f"{pk['source']} sustained cuBLAS BF16 (kernel timed inside a long step)",
                           launches=len(big), avg_launch_us=round(1000 * g_ms / max(len(big), 1), 2),
-                          all_gemms_tflops=round(all_tf, 1)),
+                          all_gemms_tflops=round(all_tf, 1),
+                          attention=dict(achieved=round(flops_attn / (attn_ms / 1000) / 1e12, 1) if attn_ms else None,
+                                         peak=pk['bf16'], frac=round(flops_attn / (attn_ms / 1000) / 1e12 / pk['bf16'],
+                                                                     4) if attn_ms else None,
+                                         unit='TFLOP/s', ms_per_tree=round(attn_ms, 3),
+                                         tflop_per_tree=round(flops_attn / 1e12, 3),
+                                         basis='algorithmic FLOPs (4 x Hq x d per visible pair, all layers as '
+                                               'specified) / summed attention launch times of one traced tree; peak: '
+                                               'burst cuBLAS BF16')),
             breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
             traced_span_ms=round(trace_span, 3), graph_replay_ms=graph_ms,
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
@@ -502,6 +548,8 @@ def main():
             clocks=clocks.summary(), init_s=round(init_s, 1))
         if cpu is not None:
             line['cpu_baseline'] = cpu
+        if parity is not None:
+            line['parity'] = parity
         print(json.dumps(line), flush=True)
     if world > 1:
         if model.peer is not None:  # every rank is done with the peers' buffers before any frees its own

@@ -315,6 +315,8 @@ def main():
                     help='replicas: one model per GPU on independent trees (weak scaling); tp: one tree, the model '
                          'sharded over all GPUs with NCCL all-reduces (strong scaling, single-tree latency)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-tp-leg', action='store_true',
+                    help='replicas at N > 1: skip the tensor-parallel latency leg that follows the replica measurement')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window'],
                     help='time one kernel alone instead of the tree forward')
     ap.add_argument('--no-split', action='store_true',
@@ -550,13 +552,78 @@ def main():
             line['cpu_baseline'] = cpu
         if parity is not None:
             line['parity'] = parity
+    if world > 1 and not tp and not args.no_tp_leg and not args.layers:
+        from morj_b200 import workloads as wl
+        one_gpu = None
+        if rank == 0:  # the latency tree on this GPU alone: the check of the sharded model's probabilities
+            t_in = wl.latency_tree(seed=0)
+            with torch.inference_mode():
+                one_gpu = np.concatenate(model.run(model.prepare(t_in['seqs'], t_in['label_ids']),
+                                                   list(range(len(t_in['seqs'])))))
+        model = preps = None  # the replica's weights go back to the allocator before the sharded model loads
+        torch.cuda.empty_cache()
+        leg = tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks)
+        if rank == 0:
+            line['tp'] = leg
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        if model.peer is not None:  # every rank is done with the peers' buffers before any frees its own
+        if model is not None and model.peer is not None:  # every rank is done with the peers' buffers first
             barrier()
             model.peer.close()
             barrier()
         dist.destroy_process_group()
+
+
+def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):
+    """The tensor-parallel latency leg of a multi-GPU run: after the replica measurement, one latency tree (8192 +
+    8 x 64 tokens) on the model sharded over all `world` GPUs with the peer-memory exchange, checked against the
+    probabilities rank 0's replica computed for the same tree alone (`one_gpu`). Returns (rank 0) the leg's figures;
+    every rank takes the same collective steps."""
+    import torch
+    import torch.distributed as dist
+    from morj_b200 import workloads as w
+    from morj_b200.lean_core import LeanGemma4
+    tree_in = w.latency_tree(seed=0)
+    seqs = list(range(len(tree_in['seqs'])))
+    barrier()
+    t_init = time.perf_counter()
+    model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD, tp_comm='peer')
+    barrier()
+    init_s = time.perf_counter() - t_init
+    with torch.inference_mode():
+        p = model.prepare_pass(model.prepare(tree_in['seqs'], tree_in['label_ids']), seqs)
+        for _ in range(args.warmup):
+            model.execute_pass(p)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            model.execute_pass(p)
+        e1.record()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        got = np.concatenate(model.run(model.prepare(tree_in['seqs'], tree_in['label_ids']), seqs))
+        model.trace = []
+        model.execute_pass(p)
+        torch.cuda.synchronize()
+        trace, model.trace = model.trace, None
+        reduce_ms = max_over_ranks(sum(a.elapsed_time(b) for kind, _, a, b in trace if kind == 'tp_reduce'))
+    barrier()
+    model.peer.close()
+    barrier()
+    del model
+    if rank != 0:
+        return None
+    return dict(gpus=world, workload='latency tree: 8192-token prefix + 8 branches x 64 tokens (seed 0, every rank)',
+                exchange='peer memory over NVLink: row-parallel partials reduced by row owners with the norm epilogues',
+                tokens=int(p['tokens']), ms_per_tree=round(ms, 3), tokens_per_s=round(p['tokens'] / (ms / 1000), 1),
+                tp_reduce_ms_per_tree=round(reduce_ms, 3), steps=args.steps, warmup=args.warmup,
+                max_abs_vs_1gpu=float(np.abs(got - one_gpu).max()), init_s=round(init_s, 1),
+                max_abs_note='one GPU and the sharded model sum the row-parallel projections in different orders; '
+                             'over 60 BF16 layers such differences reach the order of 1e-2 (the oracle against itself '
+                             'with another GEMM summation order drifts as far)',
+                timing='CUDA events over the steps on every rank, max over ranks; tp_reduce from one traced tree')
 
 
 if __name__ == '__main__':

@@ -239,6 +239,34 @@ int morj_gemm_norm_epilogue_noalloc(const void* A, long long lda, const void* B,
                                     int mode, void* x, void* h, const void* w_a, const void* scalar, const void* w_b,
                                     float eps, int has_next, void* stream);
 
+/* ---- image path (reference VisionEncoder, lean_core.py:745-781: transformers' Gemma 4 vision tower and multimodal
+ * embedder in BF16) ----------------------------------------------------------------------------------------------
+ * The tower's projections, GeGLU MLP and residual epilogues use morj_gemm_bf16, morj_attn_epilogue and
+ * morj_mlp_epilogue (layer scalar 1), its attention morj_tree_attention with one bidirectional segment per image.
+ *
+ * morj_vision_patch_prologue: pixels[i] = bf16(2 * bf16(pixels[i] - 0.5)) in place, n BF16 values (n % 8 == 0)
+ * (Gemma4VisionPatchEmbedder's rescale).
+ * morj_vision_position_add: x[r] += bf16(table[0][px] + table[1][py]) rounded to BF16, for n rows of H with patch
+ * positions (px, py) = positions[2r], positions[2r+1]; padding patches (-1, -1) are left as they are; a position
+ * outside [0, table_rows) sets the device error word (0x301). table: [2, table_rows, H] BF16.
+ * morj_vision_head_epilogue: for n rows of the fused [q | k | v] projection (heads x d each, rows ld elements
+ * apart): per head RMSNorm (q with q_norm, k with k_norm, v unweighted; BF16 output), then q and k get the 2-D rotary
+ * embedding: head dims [0, d/2) rotated by the patch's x position, [d/2, d) by its y position, pairs (i, i + d/4)
+ * within each half, angle position x inv_freq[i] (d/4 frequencies), cos/sin and every product rounded to BF16.
+ * Writes q_out, k_out, v_out as [n, heads, d]. d in {64, 128}.
+ * morj_vision_pool: out[c] = bf16(bf16(sum over r in cell_rows[cell_indptr[c] .. cell_indptr[c + 1]) of x[r] *
+ * inv_k2) * scale) for n_cells cells (Gemma4VisionPooler's position-grid average and sqrt(hidden) scale).
+ * morj_rmsnorm_rows: out[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * w), w = 1 when NULL; H <= 16384. */
+int morj_vision_patch_prologue(void* pixels, long long n, void* stream);
+int morj_vision_position_add(void* x, const int* positions, const void* table, int table_rows, int n, int H,
+                             void* stream);
+int morj_vision_head_epilogue(const void* qkv, long long ld, int n, int heads, int d, const void* q_norm,
+                              const void* k_norm, const int* positions, const float* inv_freq, float eps, void* q_out,
+                              void* k_out, void* v_out, void* stream);
+int morj_vision_pool(const void* x, int H, const int* cell_indptr, const int* cell_rows, int n_cells, float inv_k2,
+                     float scale, void* out, void* stream);
+int morj_rmsnorm_rows(const void* x, const void* w, int n, int H, float eps, void* out, void* stream);
+
 /* ---- host planner (reference Tree, lean_core.py:34-231); host memory only, no CUDA ----------------------------
  *
  * morj_tree_build: the radix layout of n_seqs token sequences (tokens concatenated, seq_indptr[n_seqs + 1]); *tree

@@ -51,6 +51,11 @@ SIGNATURES = {
     'morj_peer_reduce': [P, I, I, P, P, P, F, I, I, ctypes.c_ulonglong, P],
     'morj_peer_wait': [P, I, ctypes.c_ulonglong, P],
     'morj_gemm_norm_epilogue_noalloc': [P, LL, P, LL, I, I, I, I, P, P, P, P, P, F, I, P],
+    'morj_vision_patch_prologue': [P, LL, P],
+    'morj_vision_position_add': [P, P, P, I, I, I, P],
+    'morj_vision_head_epilogue': [P, LL, I, I, I, P, P, P, P, F, P, P, P, P],
+    'morj_vision_pool': [P, I, P, P, I, F, F, P, P],
+    'morj_rmsnorm_rows': [P, P, I, I, F, P, P],
     'morj_tree_build': [P, P, I, ctypes.POINTER(P)],
     'morj_tree_layout': [P, P, P, P, P, P, P, P],
     'morj_plan_pass': [P, P, I, P, I, I, LL, LL, I, P, LL, P, P, P, LL, P, LL, P, I, ctypes.POINTER(P)],

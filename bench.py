@@ -488,6 +488,8 @@ def main():
         if tr.get('M') == tokens and not tp and len(preps) == 1:
             traffic = tr.get('bytes_per_launch')
     attn_ms = per_kind.get('attention', {}).get('ms', 0.0)
+    alone = attention_alone(model, preps[0], top, args.steps) if (len(preps) == 1 and not tp and
+                                                                    len(preps[0]['plan']['steps']) == 1) else None
     parity = None
     if rank == 0 and args.workload == 'text' and not args.layers:
         # the bench tree's probabilities against the oracle's on the same weights and tree, recorded by
@@ -540,8 +542,10 @@ def main():
                                          unit='TFLOP/s', ms_per_tree=round(attn_ms, 3),
                                          tflop_per_tree=round(flops_attn / 1e12, 3),
                                          basis='algorithmic FLOPs (4 x Hq x d per visible pair, all layers as '
-                                               'specified) / summed attention launch times of one traced tree; peak: '
-                                               'burst cuBLAS BF16')),
+                                               'specified) / summed attention launch times of one traced tree (an '
+                                               'event pair around every launch: launch gaps included); peak: '
+                                               'burst cuBLAS BF16',
+                                         back_to_back=alone)),
             breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
             traced_span_ms=round(trace_span, 3), graph_replay_ms=graph_ms,
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
@@ -573,6 +577,52 @@ def main():
             model.peer.close()
             barrier()
         dist.destroy_process_group()
+
+
+def attention_alone(model, p, top, reps):
+    """The step's tree-attention launches (every full layer's, with the step's own tables, pool sizes and work
+    lists) back to back, without the trace's per-launch events: ms per tree and TFLOP/s. Queries and pools are seeded
+    random values of the step's shapes."""
+    import torch
+    from morj_b200 import workloads as w
+    from morj_b200.lean_core import KINDS
+    plan, st = p['plan'], p['plan']['steps'][0]
+    t, _, n_work = p['tables'][0]
+    n, hq, c = len(st['tokens']), model.hq, top['text_config']
+    d = max(dd for _, dd in model.geom.values())
+    g = torch.Generator(device=model.device).manual_seed(0)
+    q = torch.randn(n, hq * d, device=model.device, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    pools = {}
+    for kind in set(model.types):
+        kp, vp = model._kv_pool(kind, plan['cap'][KINDS[kind]])
+        kp.copy_(torch.randn(kp.shape, device=model.device, generator=g))
+        vp.copy_(torch.randn(vp.shape, device=model.device, generator=g))
+        pools[kind] = (kp, vp)
+    layers = model.types[:-1]  # the full layers (the last layer attends for its readout rows only)
+
+    def tree():
+        for kind in layers:
+            kk = KINDS[kind]
+            sliding = kind == 'sliding_attention'
+            model._attention(q[:, :hq * model.geom[kind][1]], *pools[kind], out, t, 'qo', 'kv_indptr_' + kk,
+                             'kv_indices_' + kk, len(st['qo_indptr']) - 1, int(st['n_bidir']) if sliding else 0,
+                             kind, 'work_' + kk, n_work[kk])
+    with torch.inference_mode():
+        tree()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            tree()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 4 * hq * c['head_dim'] * w.attention_pairs(plan, c['sliding_window'], layers)
+    return dict(ms_per_tree=round(ms, 3), launches=len(layers), tflop=round(flops / 1e12, 3),
+                achieved=round(flops / (ms / 1000) / 1e12, 1),
+                note='the 59 full layers\' attention launches of the bench tree, back to back, CUDA events around '
+                     'the whole sequence; seeded random queries and pools of the step\'s shapes')
 
 
 def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):

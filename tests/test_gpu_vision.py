@@ -21,7 +21,7 @@ TEXT_HIDDEN = 512
 def random_state(seed=0):
     """Checkpoint-layout tensors (`model.vision_tower.*`, `model.embed_vision.*`) for the transformers modules,
     every parameter drawn from a seeded generator: matrices N(0, 0.02), the position table N(0, 0.3), norms
-    1 + N(0, 0.1)."""
+    1 + N(0, 0.1), the q/k norms further scaled by head_dim^-1/4."""
     from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig, Gemma4VisionConfig
     from transformers.models.gemma4.modeling_gemma4 import Gemma4MultimodalEmbedder, Gemma4VisionModel
     vc = Gemma4VisionConfig(**VCFG)
@@ -32,6 +32,9 @@ def random_state(seed=0):
         for k, v in module.state_dict().items():
             if v.dim() == 1:
                 t = 1 + 0.1 * torch.randn(v.shape, generator=g)
+                if k.endswith(('q_norm.weight', 'k_norm.weight')):
+                    # attention runs with scale 1 (the q/k norms carry it): unit-variance logits, not one-hot ones
+                    t = t * v.shape[0] ** -0.25
             elif 'position_embedding_table' in k:
                 t = 0.3 * torch.randn(v.shape, generator=g)
             else:

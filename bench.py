@@ -669,7 +669,8 @@ def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):
                 exchange='peer memory over NVLink: row-parallel partials reduced by row owners with the norm epilogues',
                 tokens=int(p['tokens']), ms_per_tree=round(ms, 3), tokens_per_s=round(p['tokens'] / (ms / 1000), 1),
                 tp_reduce_ms_per_tree=round(reduce_ms, 3), steps=args.steps, warmup=args.warmup,
-                max_abs_vs_1gpu=float(np.abs(got - one_gpu).max()), init_s=round(init_s, 1),
+                max_abs_vs_1gpu=float(np.abs(got - one_gpu).max()),
+                rms_vs_1gpu=float(np.sqrt(np.mean((got - one_gpu) ** 2))), init_s=round(init_s, 1),
                 max_abs_note='one GPU and the sharded model sum the row-parallel projections in different orders; '
                              'over 60 BF16 layers such differences reach the order of 1e-2 (the oracle against itself '
                              'with another GEMM summation order drifts as far)',

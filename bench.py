@@ -591,12 +591,14 @@ def attention_alone(model, p, top, reps):
     n, hq, c = len(st['tokens']), model.hq, top['text_config']
     d = max(dd for _, dd in model.geom.values())
     g = torch.Generator(device=model.device).manual_seed(0)
-    q = torch.randn(n, hq * d, device=model.device, generator=g).to(torch.bfloat16)
+    # queries and keys as the model's q/k norms leave them (entries ~ d^-1/4, unit-variance logits at scale 1)
+    qk_std = d ** -0.25
+    q = (torch.randn(n, hq * d, device=model.device, generator=g) * qk_std).to(torch.bfloat16)
     out = torch.empty_like(q)
     pools = {}
     for kind in set(model.types):
         kp, vp = model._kv_pool(kind, plan['cap'][KINDS[kind]])
-        kp.copy_(torch.randn(kp.shape, device=model.device, generator=g))
+        kp.copy_(torch.randn(kp.shape, device=model.device, generator=g) * qk_std)
         vp.copy_(torch.randn(vp.shape, device=model.device, generator=g))
         pools[kind] = (kp, vp)
     layers = model.types[:-1]  # the full layers (the last layer attends for its readout rows only)
@@ -622,7 +624,8 @@ def attention_alone(model, p, top, reps):
     return dict(ms_per_tree=round(ms, 3), launches=len(layers), tflop=round(flops / 1e12, 3),
                 achieved=round(flops / (ms / 1000) / 1e12, 1),
                 note='the 59 full layers\' attention launches of the bench tree, back to back, CUDA events around '
-                     'the whole sequence; seeded random queries and pools of the step\'s shapes')
+                     'the whole sequence; seeded random queries and pools of the step\'s shapes, q and k scaled as the '
+                     'model\'s q/k norms leave them')
 
 
 def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):

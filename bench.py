@@ -213,7 +213,8 @@ def kernel_arm(args):
     """One kernel alone on a mid-size case (per-kernel timing and small ncu captures):
     gemm / geglu: the 31B gate-up GEMM shape (M = 2040 text-tree tokens, K = 5376) with a plain or GeGLU epilogue;
     attention / attention-window: the op-level paged tree attention (2048 + 8 x 64 tokens, 32/16 heads of 128, pages
-    of 64 through a shuffled page table), global or sliding window 1024."""
+    of 64 through a shuffled page table), global or sliding window 1024;
+    attention-text-sliding / attention-text-global: one layer's attention of the 31B text tree on its planner tables."""
     import torch
     from morj_b200 import _native as nat
     sys.path.insert(0, os.path.join(ROOT, 'tests'))
@@ -257,6 +258,37 @@ def kernel_arm(args):
         def launch():
             nat.call('morj_gemm_bf16', a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), c.stride(0), M, N, K, epi, s)
         shape = dict(M=M, N=N, K=K)
+    elif args.kernel.startswith('attention-text'):
+        # one full layer's tree attention of the 31B text tree with the planner's own tables (1500-token prefix + 9
+        # branches of 60; 32 / 16 heads of 128; sliding: window 1024), q and k scaled as the model's q/k norms leave
+        # them (unit-variance logits at scale 1)
+        from morj_b200 import workloads as w
+        from morj_b200.tree import Tree
+        sliding = args.kernel.endswith('sliding')
+        window, kk = (1024, 's') if sliding else (0, 'g')
+        tree_in = w.text_tree(0)
+        tree = Tree(tree_in['seqs'])
+        plan = tree.plan_pass(tree.pass_nodes(range(len(tree.seqs)), set()), list(range(len(tree.seqs))), 1024, 16384,
+                              8192, False)
+        st = plan['steps'][0]
+        n, hq, hk, d = len(st['tokens']), 32, 16, 128
+        g = torch.Generator(device=dev).manual_seed(0)
+        q = (torch.randn(n, hq, d, device=dev, generator=g) * d ** -0.25).to(torch.bfloat16)
+        cap = plan['cap'][kk]
+        kp = (torch.randn(cap, hk, d, device=dev, generator=g) * d ** -0.25).to(torch.bfloat16)
+        vp = torch.randn(cap, hk, d, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        qo = np.asarray(st['qo_indptr'], np.int32)
+        kvp = np.asarray(st['kv_indptr_' + kk], np.int32)
+        work = nat.attention_work(qo, kvp, 0, hq, hk, window)
+        t = [torch.as_tensor(x, device=dev) for x in (qo, kvp, np.asarray(st['kv_indices_' + kk], np.int32), work)]
+        flops = 4 * hq * d * w.attention_pairs(plan, 1024, ['sliding_attention' if sliding else 'full_attention'])
+
+        def launch():
+            nat.call('morj_tree_attention', q.data_ptr(), n, kp.data_ptr(), vp.data_ptr(), cap, out.data_ptr(),
+                     t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), None, len(qo) - 1, 0, hq, hk, d, 1, window,
+                     1.0, t[3].data_ptr(), len(work) // 2, s)
+        shape = dict(tokens=n, window=window, tiles=len(work) // 2)
     else:
         from attn_cases import op_level_case, unmasked_pairs
         window = 1024 if args.kernel == 'attention-window' else 0
@@ -317,7 +349,8 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-tp-leg', action='store_true',
                     help='replicas at N > 1: skip the tensor-parallel latency leg that follows the replica measurement')
-    ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window'],
+    ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window',
+                                         'attention-text-sliding', 'attention-text-global'],
                     help='time one kernel alone instead of the tree forward')
     ap.add_argument('--no-split', action='store_true',
                     help='no split-tile workspace registered (every GEMM tile computed whole)')

@@ -30,7 +30,6 @@ enum DeviceError : int {
   kErrTimeoutPeerRows = 0x105,
   kErrTimeoutGemmSplit = 0x106,
   kErrTimeoutAttention = 0x201,
-  kErrTimeoutRows = 0x202,
   kErrBadIndex = 0x301,
   kErrBadAlignment = 0x302,
 };

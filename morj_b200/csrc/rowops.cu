@@ -215,130 +215,6 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
   }
 }
 
-// ---- the residual epilogues, persistent and staged through shared memory -----------------------------------------
-// The same math as attn_epilogue_kernel (MODE 0) and mlp_epilogue_kernel (MODE 1), bit for bit, organised for HBM
-// bandwidth: a persistent grid (two CTAs per SM) walks the rows, and each CTA keeps a ring of EPI_STAGES
-// shared-memory stages, each holding one row's two inputs (o or d, and x) brought in by two 1D bulk copies
-// (cp.async.bulk) that complete on the stage's mbarrier. A CTA computes one row while the next two rows' reads are in
-// flight, so there is no wave tail and no CTA waits on HBM once per row. Thread 0 issues the copies and waits
-// (bounded) on each stage; its verdict reaches the CTA through shared memory before anyone reads the stage, so a wait
-// that runs out ends every thread's loop at the same row (after thread 0 has waited, bounded, for the copies still in
-// flight into this CTA's shared memory).
-constexpr int EPI_STAGES = 3;
-constexpr int EPI_CTAS_PER_SM = 2;
-
-MORJ_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
-
-template <int VPT, int MODE>
-__global__ void __launch_bounds__(THREADS, EPI_CTAS_PER_SM) residual_epilogue_kernel(
-    const __nv_bfloat16* __restrict__ a, __nv_bfloat16* x, __nv_bfloat16* h_out,
-    const __nv_bfloat16* __restrict__ w_post, const __nv_bfloat16* __restrict__ scalar,
-    const __nv_bfloat16* __restrict__ w_next, int n, int H, float eps, int has_next) {
-  extern __shared__ __align__(128) uint8_t stage_mem[];
-  __shared__ float red[32];
-  __shared__ __align__(8) unsigned long long bars[EPI_STAGES];
-  __shared__ int abort_s, ok_s;
-  const uint32_t row_bytes = (uint32_t)H * 2;
-  const uint32_t sb = smem_u32(stage_mem);
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < EPI_STAGES; ++i) mbar_init(smem_u32(&bars[i]), 1);
-    abort_s = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_wait();  // the previous kernel on the stream has completed
-  pdl_trigger();
-  const int mine = n > (int)blockIdx.x ? (n - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  int issued = 0;  // (thread 0) rows of this CTA whose copies have been issued
-  auto issue = [&](int j) {
-    const size_t row = blockIdx.x + (size_t)j * gridDim.x;
-    const int st = j % EPI_STAGES;
-    const uint32_t bar = smem_u32(&bars[st]), dst = sb + (uint32_t)st * 2 * row_bytes;
-    mbar_arrive_expect_tx(bar, 2 * row_bytes);
-    bulk_load(dst, a + row * H, row_bytes, bar);
-    bulk_load(dst + row_bytes, x + row * H, row_bytes, bar);
-  };
-  if (threadIdx.x == 0)
-    for (; issued < min(EPI_STAGES, mine); ++issued) issue(issued);
-  const float sc = MODE == 1 ? __bfloat162float(scalar[0]) : 1.f;
-  int j = 0;
-  for (; j < mine; ++j) {
-    const int st = j % EPI_STAGES;
-    if (threadIdx.x == 0) ok_s = mbar_wait(smem_u32(&bars[st]), (j / EPI_STAGES) & 1, &abort_s, kErrTimeoutRows);
-    __syncthreads();
-    if (!ok_s) break;
-    const size_t base = (blockIdx.x + (size_t)j * gridDim.x) * H;
-    const uint8_t* a_row = stage_mem + (size_t)st * 2 * row_bytes;
-    const uint8_t* x_row = a_row + row_bytes;
-    uint4 a_raw[VPT], x_raw[VPT];
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int c = (threadIdx.x + k * THREADS) * 8;
-      if (c < H) {
-        a_raw[k] = *reinterpret_cast<const uint4*>(a_row + c * 2);
-        x_raw[k] = *reinterpret_cast<const uint4*>(x_row + c * 2);
-        float av[8];
-        unpack8(a_raw[k], av);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss += av[e] * av[e];
-      }
-    }
-    const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
-    float ss2 = 0.f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int c = (threadIdx.x + k * THREADS) * 8;
-      if (c < H) {
-        float av[8], xv[8], wv[8];
-        unpack8(a_raw[k], av);
-        unpack8(x_raw[k], xv);
-        unpack8(__ldg(reinterpret_cast<const uint4*>(w_post + c)), wv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float an = bf16_round(av[e] * inv1 * wv[e]);
-          if (MODE == 0) {
-            xv[e] = bf16_round(xv[e] + an);  // the new residual
-          } else {
-            const float xa = bf16_round(xv[e] + an);
-            xv[e] = bf16_round(xa * sc);
-          }
-          ss2 += xv[e] * xv[e];
-        }
-        x_raw[k] = pack8(xv);
-        *reinterpret_cast<uint4*>(x + base + c) = x_raw[k];
-      }
-    }
-    if (MODE == 0 || has_next) {
-      const __nv_bfloat16* w_b = w_next;
-      const float inv2 = 1.0f / sqrtf(block_sum(ss2, red) / H + eps);
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int c = (threadIdx.x + k * THREADS) * 8;
-        if (c < H) {
-          float xv[8], wv[8], hv[8];
-          unpack8(x_raw[k], xv);
-          unpack8(__ldg(reinterpret_cast<const uint4*>(w_b + c)), wv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) hv[e] = xv[e] * inv2 * wv[e];
-          store8(h_out + base + c, hv);
-        }
-      }
-    }
-    __syncthreads();  // every thread is done with stage st
-    if (threadIdx.x == 0 && issued < mine) {
-      fence_proxy_async_smem();  // the reads above come before the copy that overwrites the stage
-      issue(issued++);
-    }
-  }
-  if (j < mine && threadIdx.x == 0)  // a wait ran out: let the copies still in flight land before the CTA exits
-    for (int q = j; q < issued; ++q) mbar_wait_landed(smem_u32(&bars[q % EPI_STAGES]), (q / EPI_STAGES) & 1);
-}
-
 // ---- q/k/v head norm + RoPE + scatter to the packed q and the K/V pools ------------------------------------------
 // one warp per head; lane l holds elements [l*E, l*E + E) of each half (E = D / 64)
 template <int D>
@@ -567,39 +443,6 @@ extern "C" int morj_embed_rmsnorm(const int* tokens, const int* feature_row, con
   return st;
 }
 
-namespace morj {
-namespace rows {
-// The staged epilogues hold EPI_STAGES rows x 2 inputs in shared memory; rows must start on 16-byte boundaries for the
-// bulk copies (H a multiple of 8 and 16-byte aligned bases). Wider rows take the one-CTA-per-row kernels.
-inline bool staged_fits(int H, const void* a, const void* x) {
-  return (size_t)EPI_STAGES * 4 * H <= 96 * 1024 && H % 8 == 0 &&
-         ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
-}
-
-template <int MODE>
-int launch_staged(const void* a, void* x, void* h_out, const void* w_post, const void* scalar, const void* w_next,
-                  int n, int H, float eps, int has_next, cudaStream_t s) {
-  const size_t smem = (size_t)EPI_STAGES * 4 * H;
-  const unsigned grid = (unsigned)std::min(n, num_sms() * EPI_CTAS_PER_SM);
-  int st = MORJ_OK;
-  MORJ_VPT_SWITCH(H, {
-    static bool configured = false;
-    if (!configured) {
-      const cudaError_t e = cudaFuncSetAttribute(residual_epilogue_kernel<V, MODE>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      configured = true;
-    }
-    st = launch_pdl("residual_epilogue_kernel", residual_epilogue_kernel<V, MODE>, dim3(grid), dim3(THREADS), smem,
-                    s, (const __nv_bfloat16*)a, (__nv_bfloat16*)x, (__nv_bfloat16*)h_out,
-                    (const __nv_bfloat16*)w_post, (const __nv_bfloat16*)scalar, (const __nv_bfloat16*)w_next, n, H,
-                    eps, has_next);
-  });
-  return st;
-}
-}  // namespace rows
-}  // namespace morj
-
 extern "C" int morj_attn_epilogue(const void* o, void* x, void* h_out, const void* w_post, const void* w_pre, int n,
                                   int H, float eps, void* stream) {
   if (n == 0) return MORJ_OK;
@@ -607,8 +450,6 @@ extern "C" int morj_attn_epilogue(const void* o, void* x, void* h_out, const voi
     return set_error(MORJ_ERR_ARG, "morj_attn_epilogue: bad arguments (n=%d H=%d)", n, H);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int st = MORJ_OK;
-  if (rows::staged_fits(H, o, x))
-    return rows::launch_staged<0>(o, x, h_out, w_post, nullptr, w_pre, n, H, eps, 1, s);
   MORJ_VPT_SWITCH(H, (st = launch_pdl("attn_epilogue_kernel", rows::attn_epilogue_kernel<V>, dim3(n),
                                       dim3(rows::THREADS), 0, s, (const __nv_bfloat16*)o, (__nv_bfloat16*)x,
                                       (__nv_bfloat16*)h_out, (const __nv_bfloat16*)w_post,
@@ -623,8 +464,6 @@ extern "C" int morj_mlp_epilogue(const void* d, void* x, void* h_out, const void
     return set_error(MORJ_ERR_ARG, "morj_mlp_epilogue: bad arguments (n=%d H=%d)", n, H);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int st = MORJ_OK;
-  if (rows::staged_fits(H, d, x))
-    return rows::launch_staged<1>(d, x, h_out, w_post, scalar, w_next, n, H, eps, has_next, s);
   MORJ_VPT_SWITCH(H, (st = launch_pdl("mlp_epilogue_kernel", rows::mlp_epilogue_kernel<V>, dim3(n),
                                       dim3(rows::THREADS), 0, s, (const __nv_bfloat16*)d, (__nv_bfloat16*)x,
                                       (__nv_bfloat16*)h_out, (const __nv_bfloat16*)w_post,

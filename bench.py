@@ -331,6 +331,71 @@ def kernel_arm(args):
         ws.close()
 
 
+def vision_arm(args):
+    """The image path: `args.images` images (random pixels, 896 x 896, the processor's default 280 soft tokens each)
+    through `morj_b200.vision.VisionTower` and, on the same GPU, through the reference's own path (transformers'
+    Gemma4VisionModel + Gemma4MultimodalEmbedder in BF16 with SDPA attention, as `lean_core.py:752-781` runs them),
+    transformers' default Gemma 4 vision config with seeded random weights, text hidden 5376. Prints ms per batch of
+    both and the soft tokens' relative difference."""
+    import torch
+    from PIL import Image
+    from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig, Gemma4VisionConfig
+    from transformers.models.gemma4.image_processing_gemma4 import Gemma4ImageProcessor
+    from transformers.models.gemma4.modeling_gemma4 import Gemma4MultimodalEmbedder, Gemma4VisionModel
+    from morj_b200.vision import VisionTower
+    dev = torch.device('cuda', 0)
+    vc = Gemma4VisionConfig()
+    vc._attn_implementation = 'sdpa'
+    tower = Gemma4VisionModel(vc).to(torch.bfloat16)
+    embedder = Gemma4MultimodalEmbedder(vc, Gemma4TextConfig(hidden_size=5376)).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(0)
+    state = {}
+    for prefix, module in (('model.vision_tower.', tower), ('model.embed_vision.', embedder)):
+        for k, v in module.state_dict().items():
+            t = (1 + 0.1 * torch.randn(v.shape, generator=g)) if v.dim() == 1 else torch.randn(v.shape, generator=g) * (
+                0.3 if 'position_embedding_table' in k else 0.02)
+            if k.endswith(('q_norm.weight', 'k_norm.weight')):
+                t = t * v.shape[0] ** -0.25
+            state[prefix + k] = t.to(torch.bfloat16)
+        module.load_state_dict({k[len(prefix):]: v for k, v in state.items() if k.startswith(prefix)}, strict=False)
+    tower, embedder = tower.to(dev).eval(), embedder.to(dev).eval()
+    vcfg = dict(vc.to_dict(), rope_parameters=vc.rope_parameters)
+    ours = VisionTower(vcfg, 5376, lambda k: state[k], dev)
+    rng = np.random.default_rng(0)
+    imgs = [Image.fromarray((rng.random((896, 896, 3)) * 255).astype(np.uint8)) for _ in range(args.images)]
+    p = Gemma4ImageProcessor()(imgs, return_tensors='pt')
+    pv, pos = p['pixel_values'], p['image_position_ids']
+
+    def ref():
+        with torch.inference_mode():
+            h = tower(pixel_values=pv.to(dev, torch.bfloat16), pixel_position_ids=pos.to(dev)).last_hidden_state
+            return embedder(inputs_embeds=h).reshape(-1, 5376)
+
+    def mine():
+        return ours.forward(pv, pos)[0]
+
+    out = {}
+    for name, fn in (('reference_transformers', ref), ('morj_b200', mine)):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = dict(ms_per_batch=round(e0.elapsed_time(e1) / args.steps, 3))
+        out[name + '_result'] = r.float()
+    diff = float((out.pop('morj_b200_result') - out['reference_transformers_result']).norm() /
+                 out.pop('reference_transformers_result').norm())
+    print(json.dumps(dict(kernel='vision', images=len(imgs), patches_per_image=int(pv.shape[1]),
+                          soft_tokens=int(p['num_soft_tokens_per_image'].sum()), config='Gemma4VisionConfig() defaults',
+                          relative_difference=round(diff, 5), speedup=round(
+                              out['reference_transformers']['ms_per_batch'] / out['morj_b200']['ms_per_batch'], 2),
+                          **out)), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -350,16 +415,19 @@ def main():
     ap.add_argument('--no-tp-leg', action='store_true',
                     help='replicas at N > 1: skip the tensor-parallel latency leg that follows the replica measurement')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window',
-                                         'attention-text-sliding', 'attention-text-global'],
+                                         'attention-text-sliding', 'attention-text-global', 'vision'],
                     help='time one kernel alone instead of the tree forward')
     ap.add_argument('--no-split', action='store_true',
                     help='no split-tile workspace registered (every GEMM tile computed whole)')
     ap.add_argument('--force', type=lambda v: int(v, 0), default=0,
                     help='kernel mode: or-ed into the GEMM epilogue (0x100 SM-pair kernel, 0x200 one-CTA kernel)')
+    ap.add_argument('--images', type=int, default=8, help='--kernel vision: images per batch')
     ap.add_argument('--m', type=int, default=2040)
     ap.add_argument('--n', type=int, default=43008)
     ap.add_argument('--k', type=int, default=5376)
     args = ap.parse_args()
+    if args.kernel == 'vision':
+        return vision_arm(args)
     if args.kernel:
         return kernel_arm(args)
     rank = int(os.environ.get('RANK', 0))

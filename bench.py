@@ -667,7 +667,10 @@ def main():
                                                    list(range(len(t_in['seqs'])))))
         model = preps = None  # the replica's weights go back to the allocator before the sharded model loads
         torch.cuda.empty_cache()
-        leg = tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks)
+        try:
+            leg = tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks)
+        except Exception as error:  # (every rank fails the same way: the pass protocol shares device errors)
+            leg = dict(gpus=world, error=f'{type(error).__name__}: {error}')
         if rank == 0:
             line['tp'] = leg
     if rank == 0:

@@ -132,8 +132,8 @@ def bench_config(args, world, desc, tokens, flops):
     """The `config` object of the JSON line; both arms print the same one for the same arguments."""
     tp = args.mode == 'tp' and world > 1
     par = (f'replicas x{world} (independent trees, no collective)' if not tp else
-           f'tensor parallel x{world} (O/down partial rows read by their row owners over NVLink, reduced with the '
-           f'epilogues)' if args.tp_comm == 'peer' else f'tensor parallel x{world} (NCCL all-reduce after O and down)')
+           f'tensor parallel x{world} (O/down partial rows stored by the GEMMs into their row owners\' memory over '
+           f'NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else f'tensor parallel x{world} (NCCL all-reduce after O and down)')
     work = (f'31B-class Gemma-style decoder, {desc}' if not args.layers else
             f'31B-class Gemma-style decoder cut to {args.layers} layers (profiling), {desc}')
     return dict(workload=work, tokens=tokens, parallelism=par,
@@ -214,7 +214,8 @@ def kernel_arm(args):
     gemm / geglu: the 31B gate-up GEMM shape (M = 2040 text-tree tokens, K = 5376) with a plain or GeGLU epilogue;
     attention / attention-window: the op-level paged tree attention (2048 + 8 x 64 tokens, 32/16 heads of 128, pages
     of 64 through a shuffled page table), global or sliding window 1024;
-    attention-text-sliding / attention-text-global: one layer's attention of the 31B text tree on its planner tables."""
+    attention-text-sliding / attention-text-global: one layer's attention of the 31B text tree on its planner tables;
+    peer-reduce: one tensor-parallel site's owner reduction on the latency tree's rows, `--world` ranks emulated."""
     import torch
     from morj_b200 import _native as nat
     sys.path.insert(0, os.path.join(ROOT, 'tests'))
@@ -250,14 +251,18 @@ def kernel_arm(args):
     elif args.kernel in ('gemm', 'geglu'):
         M, N, K = args.m, args.n, args.k
         a = torch.randn(M, K, device=dev).to(torch.bfloat16)
-        b = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+        # launches cycle through enough copies of the weights to exceed L2 (126 MB), so each reads them from HBM
+        bs = [(torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16) for _ in range(-(-300_000_000 // (2 * N * K)))]
         epi = (nat.EPI_GEGLU if args.kernel == 'geglu' else nat.EPI_STORE) | args.force
         c = torch.empty(M, N // 2 if args.kernel == 'geglu' else N, device=dev, dtype=torch.bfloat16)
         flops = 2 * M * N * K
+        turn = [0]
 
         def launch():
+            b = bs[turn[0] % len(bs)]
+            turn[0] += 1
             nat.call('morj_gemm_bf16', a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), c.stride(0), M, N, K, epi, s)
-        shape = dict(M=M, N=N, K=K)
+        shape = dict(M=M, N=N, K=K, weight_copies=len(bs))
     elif args.kernel.startswith('attention-text'):
         # one full layer's tree attention of the 31B text tree with the planner's own tables (1500-token prefix + 9
         # branches of 60; 32 / 16 heads of 128; sliding: window 1024), q and k scaled as the model's q/k norms leave
@@ -289,6 +294,37 @@ def kernel_arm(args):
                      t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), None, len(qo) - 1, 0, hq, hk, d, 1, window,
                      1.0, t[3].data_ptr(), len(work) // 2, s)
         shape = dict(tokens=n, window=window, tiles=len(work) // 2)
+    elif args.kernel == 'peer-reduce':
+        # the owner's reduction of one tensor-parallel site (post-attention epilogue) on the latency tree's rows
+        # (8192 + 8 x 64, hidden 5376), the `args.world` ranks of a group emulated on this GPU: every rank's
+        # row-parallel GEMM has delivered its partials into the owners' inboxes once, so the timed launches of rank
+        # 0's reduction find their counters met and read and write this GPU's memory only
+        import ctypes
+        from morj_b200.tp import exchange_layout, owner, partial_target
+        world, n, H, k = args.world, 8704, 5376, 64
+        lay = exchange_layout(world, H, n)
+        bufs = [torch.zeros(lay['nbytes'], dtype=torch.uint8, device=dev) for _ in range(world)]
+        descs = []
+        for r in range(world):
+            d = nat.PeerDesc()
+            d.world, d.rank, d.max_blocks, d.hidden = world, r, lay['max_blocks'], H
+            for q in range(world):
+                for name, (off, _) in lay['regions'].items():
+                    getattr(d, name)[q] = bufs[q].data_ptr() + off
+            descs.append(d)
+        g = torch.Generator(device=dev).manual_seed(0)
+        wn = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16)
+        for r in range(world):
+            a = torch.randn(n, k, device=dev, generator=g).to(torch.bfloat16)
+            wt = (torch.randn(H, k, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+            nat.call('morj_gemm_bf16_peer', a.data_ptr(), k, wt.data_ptr(), k, n, H, k, ctypes.addressof(descs[r]), s)
+        d0, tgt = ctypes.addressof(descs[0]), partial_target(1, world, H)
+        owned = sum(min(n, (b + 1) * 128) - b * 128 for b in range(-(-n // 128)) if owner(b, world) == 0)
+        nbytes = owned * H * 2 * (world + 2 + world)  # every rank's partial, x read and written, h to every rank
+
+        def launch():
+            nat.call('morj_peer_reduce', d0, 0, n, wn.data_ptr(), None, wn.data_ptr(), 1e-6, 1, 0, tgt, s)
+        shape = dict(rows=n, owned_rows=owned, hidden=H, world=world)
     else:
         from attn_cases import op_level_case, unmasked_pairs
         window = 1024 if args.kernel == 'attention-window' else 0
@@ -322,10 +358,21 @@ def kernel_arm(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     pk = peaks()
-    tf = flops / (ms / 1000) / 1e12
-    print(json.dumps(dict(kernel=args.kernel, shape=shape, ms=round(ms, 4), tflops=round(tf, 1),
-                          frac_of_burst_peak=round(tf / pk['bf16'], 4), peak_source=pk['source'],
-                          gflop=round(flops / 1e9, 2))), flush=True)
+    if args.kernel == 'peer-reduce':
+        gbs = nbytes / (ms / 1000) / 1e9
+        print(json.dumps(dict(kernel=args.kernel, shape=shape, ms=round(ms, 4), gbs=round(gbs, 1),
+                              frac_of_copy_peak=round(gbs / pk['hbm'], 4), peak_source=pk['source'],
+                              mbytes=round(nbytes / 1e6, 1))), flush=True)
+    else:
+        tf = flops / (ms / 1000) / 1e12
+        extra = {}
+        if args.kernel in ('gemm', 'geglu'):  # operand bytes (the weights dominate at small M: HBM-bound there)
+            ob = 2 * (args.m * args.k + args.n * args.k + args.m * (args.n // 2 if args.kernel == 'geglu' else args.n))
+            extra = dict(gbs=round(ob / (ms / 1000) / 1e9, 1), frac_of_copy_peak=round(ob / (ms / 1000) / 1e9 /
+                                                                                        pk['hbm'], 4))
+        print(json.dumps(dict(kernel=args.kernel, shape=shape, ms=round(ms, 4), tflops=round(tf, 1),
+                              frac_of_burst_peak=round(tf / pk['bf16'], 4), peak_source=pk['source'],
+                              gflop=round(flops / 1e9, 2), **extra)), flush=True)
     assert nat.device_error(s) == 0
     if ws is not None:
         ws.close()
@@ -415,13 +462,15 @@ def main():
     ap.add_argument('--no-tp-leg', action='store_true',
                     help='replicas at N > 1: skip the tensor-parallel latency leg that follows the replica measurement')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window',
-                                         'attention-text-sliding', 'attention-text-global', 'vision'],
+                                         'attention-text-sliding', 'attention-text-global', 'peer-reduce',
+                                         'vision'],
                     help='time one kernel alone instead of the tree forward')
     ap.add_argument('--no-split', action='store_true',
                     help='no split-tile workspace registered (every GEMM tile computed whole)')
     ap.add_argument('--force', type=lambda v: int(v, 0), default=0,
                     help='kernel mode: or-ed into the GEMM epilogue (0x100 SM-pair kernel, 0x200 one-CTA kernel)')
     ap.add_argument('--images', type=int, default=8, help='--kernel vision: images per batch')
+    ap.add_argument('--world', type=int, default=2, help='--kernel peer-reduce: ranks of the emulated group')
     ap.add_argument('--m', type=int, default=2040)
     ap.add_argument('--n', type=int, default=43008)
     ap.add_argument('--k', type=int, default=5376)
@@ -554,8 +603,10 @@ def main():
             barrier()
             graph_ms = round(e4.elapsed_time(e5) / args.steps, 3)
             del graph
-        # ---- one traced step (CUDA events around every kernel) for the per-kernel roofline -----------------------
+        # ---- one traced step (CUDA events around every kernel) for the per-kernel roofline: the stream is held by a
+        # device-side sleep while the host queues the whole step, so no event pair holds host launch latency ------
         model.trace = []
+        torch.cuda._sleep(int(0.25 * 2.0e9))  # ~0.25 s at 2 GHz (longer at the power-capped clock)
         execute_all()
         torch.cuda.synchronize()
         trace, model.trace = model.trace, None
@@ -648,6 +699,9 @@ def main():
                                                'burst cuBLAS BF16',
                                          back_to_back=alone)),
             breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
+            breakdown_basis=('one traced tree: a CUDA event pair around every launch, the whole tree queued behind a '
+                             'device sleep first (no host latency inside a pair; the overlap of programmatic '
+                             'dependent launches between kernels is lost, so the sum exceeds ms_per_step)'),
             traced_span_ms=round(trace_span, 3), graph_replay_ms=graph_ms,
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
                      ms_per_step=e2e_max),

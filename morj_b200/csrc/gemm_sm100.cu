@@ -55,13 +55,16 @@ struct QkvEpi {
   __nv_bfloat16* v_pool;
 };
 
-// Operands of the partial epilogue (tensor parallelism over peer memory): the output rows go to this rank's part
-// buffer and the columns written for row block b are counted on the counter b of its owner, rank b % world.
+// Operands of the partial epilogue (tensor parallelism over peer memory): the output rows of row block b go
+// straight into the inbox of its owner, rank b % world (its part buffer, over NVLink for a peer), at inbox block
+// (b - b % world) + rank, and the columns written are counted on the owner's counter b. The owner's reduction then
+// reads every rank's partial from its own HBM, and the NVLink transfer overlaps the GEMM's later tiles.
 constexpr int EPI_PEER = 4;
 struct PeerEpi {
-  __nv_bfloat16* part;
+  __nv_bfloat16* part[MORJ_MAX_RANKS];
   unsigned long long* partials[MORJ_MAX_RANKS];
   int world;
+  int rank;
 };
 
 // Split tiles of the pair kernel. When the tiles do not fill whole waves of SM pairs, the tiles of the last one to
@@ -355,16 +358,18 @@ MORJ_DEV void store_row(uint32_t tacc, __nv_bfloat16* crow, int n_blk, bool row_
   }
 }
 
-// Partial epilogue: this thread's row of the tile goes to this rank's part buffer (the STORE epilogue's stores);
-// the tile's column count for the row block's owner is returned, to be posted by `peer_arrive`. Row blocks wholly
-// past M (the pair kernel's padding) neither store nor count.
+// Partial epilogue: this thread's row of the tile goes to the row block owner's inbox (the STORE epilogue's stores);
+// the tile's column count for the owner is returned, to be posted by `peer_arrive`. Row blocks wholly past M (the
+// pair kernel's padding) neither store nor count.
 template <int BN>
 MORJ_DEV void epilogue_peer(uint32_t tacc, int row, int n_blk, int M, int N, const PeerEpi& pe,
                             unsigned long long*& count, unsigned long long& cols) {
   const int blk = row / 128;
   if (blk * 128 >= M) return;
-  store_row<BN>(tacc, pe.part + (size_t)row * N, n_blk, row < M, N);
-  count = pe.partials[blk % pe.world] + blk;
+  const int own = blk % pe.world;
+  const size_t slot = (size_t)(blk - own + pe.rank) * 128 + (row & 127);
+  store_row<BN>(tacc, pe.part[own] + slot * N, n_blk, row < M, N);
+  count = pe.partials[own] + blk;
   cols = (unsigned long long)(min(N, (n_blk + 1) * BN) - n_blk * BN);
 }
 
@@ -881,7 +886,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   pdl_trigger();
 
   const int num_m = (M + 2 * BM - 1) / (2 * BM), num_n = (N + BN - 1) / BN;
-  const int tiles = num_m * num_n;
   const int kblocks = (K + BK - 1) / BK;
   const uint32_t smem_base = smem_u32(smem);
   const int cluster = blockIdx.x / 2, n_clusters = gridDim.x / 2;
@@ -1026,6 +1030,254 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Skinny kernel, M <= 16 activation rows (the last layer's readout rows): C = X . W^T is computed as W . X^T, so the
+// weights are the MMA's A operand (128 weight rows per tile, M = 128) and stream through the SMs once, and the
+// activation rows are its B operand (N = 16; rows past M are zero-filled by TMA). The (tile, k-block) units, tile-major,
+// are cut into one contiguous range per CTA, one CTA per SM, so every SM streams the same number of weight bytes
+// whatever the tile count (the 42 tiles of a 5376-wide projection would leave 106 of 148 SMs idle). A range's piece of
+// a tile accumulates in TMEM and goes to the workspace as an FP32 [128 x 16] partial; the piece that completes a tile
+// (an atomic count per tile, or per gate/up tile pair with the GeGLU epilogue) adds the tile's pieces in k order
+// (so the sum does not depend on arrival order), rounds, and stores the output columns of the M rows.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int SK_N = 16;
+constexpr int SK_B_BYTES = SK_N * BK * 2;
+constexpr int SK_STAGE = A_BYTES + SK_B_BYTES;  // 18 KB, a multiple of the 1 KB swizzle atom
+constexpr int SK_STAGES = 11;
+constexpr int SK_SMEM = SK_STAGES * SK_STAGE + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SK_SLOT_FLOATS = BM * SK_N;  // one piece: [128 weight rows][16 activation rows] FP32
+constexpr int SK_TMEM_COLS = 32;           // two 16-column accumulators
+constexpr uint32_t SK_IDESC = idesc_bf16(BM, SK_N);
+
+struct Skinny {
+  float* slots;      // [tiles][pmax][SK_SLOT_FLOATS]
+  unsigned* counts;  // per tile (store) or tile pair (GeGLU): pieces arrived this launch; 0 at rest
+  int pmax;
+};
+
+// The CTA whose range holds unit u when `units` units are cut into `ctas` ranges [units * g / ctas, ...).
+__host__ __device__ inline int sk_owner(long long u, int ctas, long long units) {
+  return (int)(((u + 1) * ctas + units - 1) / units) - 1;
+}
+__host__ __device__ inline int sk_pieces(int t, int kb, int ctas, long long units) {
+  return sk_owner((long long)t * kb + kb - 1, ctas, units) - sk_owner((long long)t * kb, ctas, units) + 1;
+}
+
+MORJ_DEV void sk_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }  // the four epilogue warps
+
+// Sum of tile t's pieces for weight row r (k order).
+MORJ_DEV void sk_sum(const Skinny& sk, int t, int r, int pieces, float (&acc)[SK_N]) {
+#pragma unroll
+  for (int m = 0; m < SK_N; ++m) acc[m] = 0.f;
+  for (int q = 0; q < pieces; ++q) {
+    const float4* src =
+        reinterpret_cast<const float4*>(sk.slots + ((size_t)t * sk.pmax + q) * SK_SLOT_FLOATS + r * SK_N);
+#pragma unroll
+    for (int v = 0; v < SK_N / 4; ++v) {
+      const float4 x = __ldcg(src + v);
+      acc[4 * v] += x.x;
+      acc[4 * v + 1] += x.y;
+      acc[4 * v + 2] += x.z;
+      acc[4 * v + 3] += x.w;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                  __nv_bfloat16* __restrict__ C, long long ldc, int M, int N, int K, const Skinny sk) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SK_STAGES * SK_STAGE);
+  // bars: full[SK_STAGES], empty[SK_STAGES], acc_full[2], acc_empty[2], done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SK_STAGES + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + SK_STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * SK_STAGES), acce0 = smem_u32(bars + 2 * SK_STAGES + 2);
+  const uint32_t done0 = smem_u32(bars + 2 * SK_STAGES + 4);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SK_STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 128);
+    }
+    mbar_init(done0, 1);
+    *abort = 0;
+    fence_mbar_init();
+    tma_prefetch(&map_w);
+    tma_prefetch(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), SK_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // (set-up above touches no global memory) the previous kernel on the stream has completed
+  pdl_trigger();
+
+  const int tiles = (N + BM - 1) / BM, kb = (K + BK - 1) / BK;
+  const long long units = (long long)tiles * kb;
+  const int ctas = (int)gridDim.x;
+  const long long lo = units * blockIdx.x / ctas, hi = units * (blockIdx.x + 1) / ctas;  // lo < hi: ctas <= units
+  const int t_first = (int)(lo / kb), t_last = (int)((hi - 1) / kb);
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();  // every weight byte is read once
+      const uint64_t pol_x = policy_evict_last();   // the activation rows are read by every CTA
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = t_first; t <= t_last && ok && !*abort; ++t) {
+        const int k0 = (int)(lo > (long long)t * kb ? lo - (long long)t * kb : 0);
+        const int k1 = (int)(hi < (long long)(t + 1) * kb ? hi - (long long)t * kb : kb);
+        for (int k = k0; k < k1; ++k) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kErrTimeoutGemmProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_base + stage * SK_STAGE;
+          mbar_arrive_expect_tx(full0 + 8 * stage, SK_STAGE);
+          tma_load_2d(sa, &map_w, full0 + 8 * stage, k * BK, t * BM, pol_w);
+          tma_load_2d(sa + A_BYTES, &map_x, full0 + 8 * stage, k * BK, 0, pol_x);
+          ++issued;
+          if (++stage == SK_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // no copy may still be in flight when the CTA exits: wait for the last fills to land
+      const int pending = issued < SK_STAGES ? issued : SK_STAGES;
+      for (int j = 1; j <= pending; ++j) {
+        const int s = (stage - j + SK_STAGES) % SK_STAGES;
+        const uint32_t ph = (stage - j >= 0) ? phase : (phase ^ 1);
+        mbar_wait_landed(full0 + 8 * s, ph);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = t_first; t <= t_last && ok; ++t) {
+        const int k0 = (int)(lo > (long long)t * kb ? lo - (long long)t * kb : 0);
+        const int k1 = (int)(hi < (long long)(t + 1) * kb ? hi - (long long)t * kb : kb);
+        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kErrTimeoutGemmMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * SK_N;
+        for (int k = k0; k < k1; ++k) {
+          if (!mbar_wait(full0 + 8 * stage, phase, abort, kErrTimeoutGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * SK_STAGE;
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)
+            umma_bf16(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sa + A_BYTES + 32 * j), SK_IDESC,
+                      (k != k0) || j != 0);
+          umma_commit(empty0 + 8 * stage);
+          if (++stage == SK_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(accf0 + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // TMEM is freed below only after every MMA issued here has completed
+      umma_commit(done0);
+      mbar_wait_landed(done0, 0);
+    }
+  } else {
+    // epilogue warps 2..5: warp w reads TMEM lanes 32 (w % 4) .. + 31, i.e. weight row r of the tile
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = t_first; t <= t_last; ++t) {
+      int ok = lane == 0 ? (int)mbar_wait(accf0 + 8 * acc, acc_phase, abort, kErrTimeoutGemmEpilogue) : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;  // (a phase that completed completes for every warp: all four leave at the same tile)
+      tc_fence_after();
+      uint32_t v[SK_N];
+      tmem_ld16(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * SK_N, v);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(acce0 + 8 * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+      const int first = sk_owner((long long)t * kb, ctas, units);
+      float4* slot = reinterpret_cast<float4*>(sk.slots + ((size_t)t * sk.pmax + (blockIdx.x - first)) * SK_SLOT_FLOATS +
+                                               r * SK_N);
+#pragma unroll
+      for (int q = 0; q < SK_N / 4; ++q)
+        slot[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                              __uint_as_float(v[4 * q + 3]));
+      __threadfence();
+      sk_bar();
+      const int c = EPI == MORJ_EPI_GEGLU ? t / 2 : t;
+      if (warp == 2 && lane == 0) {
+        int expected = sk_pieces(t, kb, ctas, units);
+        if constexpr (EPI == MORJ_EPI_GEGLU) expected += sk_pieces(t ^ 1, kb, ctas, units);
+        *last = atomicAdd(sk.counts + c, 1u) + 1 == (unsigned)expected;
+      }
+      sk_bar();
+      if (*last) {
+        __threadfence();
+        if constexpr (EPI == MORJ_EPI_GEGLU) {
+          // gate rows: tile 2c, up rows: tile 2c + 1 -> output columns [128 c, 128 c + 128)
+          float g[SK_N], u[SK_N];
+          const int tg = 2 * c;
+          sk_sum(sk, tg, r, sk_pieces(tg, kb, ctas, units), g);
+          sk_sum(sk, tg + 1, r, sk_pieces(tg + 1, kb, ctas, units), u);
+          const int col = c * BM + r;
+          if (col < N / 2) {
+#pragma unroll
+            for (int m = 0; m < SK_N; ++m)
+              if (m < M) C[(size_t)m * ldc + col] = __float2bfloat16(gelu_tanh(bf16_round(g[m])) * bf16_round(u[m]));
+          }
+        } else {
+          float a[SK_N];
+          sk_sum(sk, t, r, sk_pieces(t, kb, ctas, units), a);
+          const int col = t * BM + r;
+          if (col < N) {
+#pragma unroll
+            for (int m = 0; m < SK_N; ++m)
+              if (m < M) C[(size_t)m * ldc + col] = __float2bfloat16(a[m]);
+          }
+        }
+        if (warp == 2 && lane == 0) sk.counts[c] = 0;  // every piece of this count has arrived: back to rest
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, SK_TMEM_COLS);
   }
 }
 
@@ -1176,6 +1428,44 @@ static int launch2(const void* A, long long lda, const void* B, long long ldb, v
 // shapes: 128 + BN rows for one CTA, 128 + BN / 2 per SM for the pair). With split tiles (`split`: a workspace is
 // registered for the stream) the pair kernel's last waves are shared out evenly, so its wave count is fractional
 // once there are more tiles than pairs. Ties go to the pair kernel, then to the wider tile.
+// The skinny kernel for M <= 16 rows when a workspace is registered for the stream and the partials fit it;
+// returns kSkinnyNo when it does not apply (the tiled kernels run instead).
+constexpr int kSkinnyNo = -1;
+template <int EPI>
+static int launch_skinny(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M,
+                         int N, int K, cudaStream_t stream) {
+  void* ws = workspace_for(stream);
+  if (M > SK_N || !ws) return kSkinnyNo;
+  const int tiles = (N + BM - 1) / BM, kb = (K + BK - 1) / BK;
+  const long long units = (long long)tiles * kb;
+  const int ctas = units < num_sms() ? (int)units : num_sms();
+  int pmax = 1;
+  for (int t = 0; t < tiles; ++t) {
+    const int p = sk_pieces(t, kb, ctas, units);
+    pmax = p > pmax ? p : pmax;
+  }
+  const size_t pairs = num_sms() / 2;
+  if ((size_t)tiles * pmax * SK_SLOT_FLOATS * sizeof(float) > pairs * kSlotBytesPerPair ||
+      (size_t)tiles * sizeof(unsigned) > pairs * kFlagBytesPerPair)
+    return kSkinnyNo;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(skinny_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+    if (e != cudaSuccess) return set_error(MORJ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  CUtensorMap mw, mx;
+  int st = make_map(&mw, B, N, K, ldb, BM);
+  if (st) return st;
+  st = make_map(&mx, A, M, K, lda, SK_N);
+  if (st) return st;
+  // the split-tile workspace's slot area holds the partials, its flag area the counts (both idle between launches)
+  const Skinny sk{static_cast<float*>(ws),
+                  reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pairs * kSlotBytesPerPair), pmax};
+  return launch_pdl("skinny_kernel", skinny_kernel<EPI>, dim3(ctas), dim3(THREADS), SK_SMEM, stream, mw, mx,
+                    reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K, sk);
+}
+
 struct Choice {
   int bn;
   bool pair;
@@ -1222,6 +1512,10 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
   epilogue &= 0xff;
   if (epilogue == MORJ_EPI_STORE) {
     if (N % 16 || ldc < N) return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: N must be a multiple of 16 (N=%d)", N);
+    if (!force) {
+      const int st = gemm::launch_skinny<MORJ_EPI_STORE>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      if (st != gemm::kSkinnyNo) return st;
+    }
     static const int cand[] = {256, 240, 224, 208, 192, 176, 160, 128};
     const gemm::Choice c = gemm::pick(M, N, cand, 8, force, gemm::workspace_for(s) != nullptr);
 #define MORJ_STORE_CASE(W)                                                                   \
@@ -1245,6 +1539,10 @@ extern "C" int morj_gemm_bf16(const void* A, long long lda, const void* B, long 
   if (epilogue == MORJ_EPI_GEGLU) {
     if (N % 256 || ldc < N / 2)
       return set_error(MORJ_ERR_ARG, "morj_gemm_bf16: GEGLU needs N a multiple of 256 (N=%d)", N);
+    if (!force) {
+      const int st = gemm::launch_skinny<MORJ_EPI_GEGLU>(A, lda, B, ldb, C, ldc, M, N, K, s);
+      if (st != gemm::kSkinnyNo) return st;
+    }
     static const int cand[] = {256};
     if (gemm::pick(M, N, cand, 1, force, gemm::workspace_for(s) != nullptr).pair)
       return gemm::launch2<MORJ_EPI_GEGLU, 256>(A, lda, B, ldb, C, ldc, M, N, K, s);
@@ -1260,7 +1558,7 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
   if (!A || !B || !peer || M < 0 || N <= 0 || K <= 0)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: bad pointers or sizes (M=%d N=%d K=%d)", M, N, K);
   if (peer->world < 1 || peer->world > MORJ_MAX_RANKS || peer->rank < 0 || peer->rank >= peer->world ||
-      N != peer->hidden || M > peer->max_blocks * 128)
+      peer->max_blocks % peer->world || N != peer->hidden || M > peer->max_blocks * 128)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: exchange buffers do not fit (M=%d N=%d)", M, N);
   if (N % 16 || K % 8 || lda % 8 || ldb % 8 || lda < K || ldb < K)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: N % 16, K and leading dimensions % 8 required");
@@ -1270,12 +1568,13 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
   for (int r = 0; r < peer->world; ++r) {
     if (!peer->partials[r] || (reinterpret_cast<uintptr_t>(peer->partials[r]) & 7))
       return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's counters are missing or unaligned", r);
+    if (!peer->part[r] || (reinterpret_cast<uintptr_t>(peer->part[r]) & 15))
+      return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's part buffer is missing or unaligned", r);
     pe.partials[r] = peer->partials[r];
+    pe.part[r] = reinterpret_cast<__nv_bfloat16*>(peer->part[r]);
   }
-  if (!peer->part[peer->rank] || (reinterpret_cast<uintptr_t>(peer->part[peer->rank]) & 15))
-    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: part buffer missing or unaligned");
-  pe.part = reinterpret_cast<__nv_bfloat16*>(peer->part[peer->rank]);
   pe.world = peer->world;
+  pe.rank = peer->rank;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   static const int cand[] = {256, 208, 192, 128};
   // (the widths the STORE path picks for these shapes)

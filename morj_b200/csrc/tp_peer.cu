@@ -2,16 +2,16 @@
 // hand-back of the reduced rows, replacing an NCCL all-reduce followed by replicated epilogues.
 //
 // Row block b (128 rows) belongs to rank b % world. Every rank's row-parallel GEMM (morj_gemm_bf16_peer) has stored
-// its BF16 partial rows in its own part buffer and counted the columns of block b on the owner's counter. Here the
-// owner
+// its BF16 partial rows of block b into the owner's part buffer (its inbox, at block (b - b % world) + source rank)
+// and counted the columns on the owner's counter. Here the owner
 //   1. waits (one thread per CTA, acquire at system scope, bounded) until block b's counter holds every rank's
 //      columns for this site,
-//   2. reads block b's partial rows from every rank (NVLink loads from the peers' part buffers), sums them in rank
-//      order in FP32 and rounds to BF16,
+//   2. reads block b's partial rows of every rank from its own inbox (local HBM), sums them in rank order in FP32
+//      and rounds to BF16,
 //   3. applies the post-attention or post-MLP epilogue (the math of morj_attn_epilogue / morj_mlp_epilogue) to its
 //      rows, and
 //   4. stores the new h rows (and x rows, when asked) into every rank's buffers over NVLink, then counts one row on
-//      each rank's row counter for block b (after a system fence, release at system scope).
+//      each rank's row counter for block b (after a CTA barrier, release at system scope).
 // morj_peer_wait then holds each rank's stream until all of h has arrived. Counters only grow; the host passes
 // cumulative targets, and the last CTA of every reduce pads the blocks beyond this call's rows so that every block
 // advances by the same amount per site. Plain stores and atomics to peer memory only: no multicast, no NVLS.
@@ -48,17 +48,19 @@ MORJ_DEV bool wait_at_least(const unsigned long long* p, unsigned long long targ
   }
 }
 
-constexpr int RED_ROWS = 4;  // rows per CTA (one wait, one system fence and one arrival each): many CTAs keep many
-                             // rows' remote loads in flight
-
-// One CTA per 4 rows of this rank's row blocks below n, plus one last CTA that pads the blocks past n.
-template <int VPT, int MODE>
-__global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p, int n,
-                                                            const __nv_bfloat16* __restrict__ w_a,
-                                                            const __nv_bfloat16* __restrict__ scalar,
-                                                            const __nv_bfloat16* __restrict__ w_b, float eps,
-                                                            int has_next, int push_x,
-                                                            unsigned long long partial_target) {
+// One CTA per row of this rank's row blocks below n, plus one last CTA that pads the blocks past n. The row's x
+// (this rank's own memory, written only by its own earlier kernels) is loaded before the counter wait and the ranks'
+// partials right after it, as packed BF16, two ranks at a time with the loop over ranks unrolled to W (the group
+// size rounded up to 2, 4 or 8): a runtime loop over ranks left one load round trip per rank and vector in the
+// chain, and holding all W partials at once cut the CTAs per SM to one at W = 8. The partials go through L2 only
+// (`ld.cg`): peers' GEMMs write them while this kernel runs. The row's stores are published by one barrier and the
+// release atomics that count the row (release is cumulative over the barrier, as in a stream-K fix-up's arrival);
+// a system fence in every thread stalled the kernel most of its time.
+template <int VPT, int MODE, int W>
+__global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
+    reduce_kernel(const morj_peer_t p, int n, const __nv_bfloat16* __restrict__ w_a,
+                  const __nv_bfloat16* __restrict__ scalar, const __nv_bfloat16* __restrict__ w_b, float eps,
+                  int has_next, int push_x, unsigned long long partial_target) {
   pdl_wait();  // the previous kernel on the stream has completed
   pdl_trigger();
   __shared__ float red[32];
@@ -75,31 +77,60 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
     }
     return;
   }
-  constexpr int PER_BLOCK = 128 / RED_ROWS;
-  const int blk = rank + (int)(blockIdx.x / PER_BLOCK) * world;
-  const int sub = (int)(blockIdx.x % PER_BLOCK) * RED_ROWS;
+  const int blk = rank + (int)(blockIdx.x / 128) * world;
+  const int row = blk * 128 + (int)(blockIdx.x % 128);
+  const bool live = row < n;  // rows past n in the last block only count
+  __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(p.x[rank]) + (size_t)row * H;
+  uint4 x_raw[VPT];
+  if (live) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int c = (threadIdx.x + k * ROW_THREADS) * 8;
+      if (c < H) x_raw[k] = *reinterpret_cast<const uint4*>(x + c);
+    }
+  }
   if (threadIdx.x == 0) ok_s = wait_at_least(p.partials[rank] + blk, partial_target, kErrTimeoutPeerPartials);
   __syncthreads();
   if (!ok_s) return;  // the peers' waits for this block's rows run out and report too
-  const float sc = MODE == 1 ? __bfloat162float(scalar[0]) : 1.f;
-  for (int j = 0; j < RED_ROWS; ++j) {
-    const int row = blk * 128 + sub + j;
-    if (row >= n) break;
-    __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(p.x[rank]) + (size_t)row * H;
+  if (live) {
+    // source rank s's partial of this row: inbox block blk - rank + s, the row's offset in the block
+    const __nv_bfloat16* in =
+        reinterpret_cast<const __nv_bfloat16*>(p.part[rank]) + ((size_t)(blk - rank) * 128 + (row & 127)) * H;
     float ov[VPT][8];
+#pragma unroll
+    for (int s0 = 0; s0 < W; s0 += 2) {
+      uint4 raw[2][VPT];
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int c = (threadIdx.x + k * ROW_THREADS) * 8;
+        if (c < H) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            if (s0 + j < world)
+              raw[j][k] = __ldcg(reinterpret_cast<const uint4*>(in + (size_t)(s0 + j) * 128 * H + c));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int c = (threadIdx.x + k * ROW_THREADS) * 8;
+        if (c < H) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            if (s0 + j < world) {
+              float pv[8];
+              unpack8(raw[j][k], pv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ov[k][e] = (s0 + j == 0) ? pv[e] : ov[k][e] + pv[e];  // FP32, rank order
+            }
+          }
+        }
+      }
+    }
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int c = (threadIdx.x + k * ROW_THREADS) * 8;
       if (c < H) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ov[k][e] = 0.f;
-        for (int src = 0; src < world; ++src) {
-          float pv[8];
-          load8(reinterpret_cast<const __nv_bfloat16*>(p.part[src]) + (size_t)row * H + c, pv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ov[k][e] += pv[e];
-        }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           ov[k][e] = bf16_round(ov[k][e]);  // the reduced BF16 projection
@@ -107,6 +138,7 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
         }
       }
     }
+    const float sc = MODE == 1 ? __bfloat162float(scalar[0]) : 1.f;
     const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
     float ss2 = 0.f;
 #pragma unroll
@@ -114,7 +146,7 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
       const int c = (threadIdx.x + k * ROW_THREADS) * 8;
       if (c < H) {
         float xv[8], wv[8];
-        load8(x + c, xv);
+        unpack8(x_raw[k], xv);
         load8(w_a + c, wv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -123,8 +155,10 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
           ov[k][e] = MODE == 1 ? bf16_round(xa * sc) : xa;  // the new residual
           ss2 += ov[k][e] * ov[k][e];
         }
-        for (int r = 0; r < world; ++r)
-          if (r == rank || push_x) store8(reinterpret_cast<__nv_bfloat16*>(p.x[r]) + (size_t)row * H + c, ov[k]);
+#pragma unroll
+        for (int r = 0; r < W; ++r)
+          if (r < world && (r == rank || push_x))
+            store8(reinterpret_cast<__nv_bfloat16*>(p.x[r]) + (size_t)row * H + c, ov[k]);
       }
     }
     if (MODE == 0 || has_next) {
@@ -137,15 +171,15 @@ __global__ void __launch_bounds__(ROW_THREADS) reduce_kernel(const morj_peer_t p
           load8(w_b + c, wv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) hv[e] = ov[k][e] * inv2 * wv[e];
-          for (int r = 0; r < world; ++r)
-            store8(reinterpret_cast<__nv_bfloat16*>(p.h[r]) + (size_t)row * H + c, hv);
+#pragma unroll
+          for (int r = 0; r < W; ++r)
+            if (r < world) store8(reinterpret_cast<__nv_bfloat16*>(p.h[r]) + (size_t)row * H + c, hv);
         }
       }
     }
   }
-  __threadfence_system();
-  __syncthreads();
-  if ((int)threadIdx.x < world) red_release_sys_add(p.rows[threadIdx.x] + blk, (unsigned long long)RED_ROWS);
+  __syncthreads();  // every thread's stores of this row precede the release below
+  if ((int)threadIdx.x < world) red_release_sys_add(p.rows[threadIdx.x] + blk, 1ull);
 }
 
 __global__ void __launch_bounds__(ROW_THREADS) wait_kernel(const unsigned long long* rows, int n_blocks,
@@ -158,7 +192,7 @@ __global__ void __launch_bounds__(ROW_THREADS) wait_kernel(const unsigned long l
 
 static int check_peer(const morj_peer_t* p, const char* who) {
   if (!p || p->world < 1 || p->world > MORJ_MAX_RANKS || p->rank < 0 || p->rank >= p->world || p->max_blocks <= 0 ||
-      p->hidden <= 0 || p->hidden % 8)
+      p->max_blocks % p->world || p->hidden <= 0 || p->hidden % 8)
     return set_error(MORJ_ERR_ARG, "%s: bad exchange description", who);
   for (int r = 0; r < p->world; ++r)
     if (!p->part[r] || !p->x[r] || !p->h[r] || !p->partials[r] || !p->rows[r] ||
@@ -240,21 +274,24 @@ extern "C" int morj_peer_reduce(const morj_peer_t* p, int mode, int n, const voi
   const int H = p->hidden;
   const int n_blocks = (n + 127) / 128;
   const int owned = n_blocks > p->rank ? (n_blocks - p->rank + p->world - 1) / p->world : 0;
-  const unsigned grid = (unsigned)owned * (128 / peer::RED_ROWS) + 1;
+  const unsigned grid = (unsigned)owned * 128 + 1;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const __nv_bfloat16* wa = static_cast<const __nv_bfloat16*>(w_a);
   const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(scalar);
   const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w_b);
+  const int hn = mode == 0 ? 1 : has_next;
   int st2 = MORJ_OK;
-  if (mode == 0) {
-    MORJ_VPT_SWITCH(H, (st2 = launch_pdl("peer::reduce_kernel", peer::reduce_kernel<V, 0>, dim3(grid),
-                                         dim3(ROW_THREADS), 0, s, *p, n, wa, sc, wb, eps, 1, push_x,
-                                         partial_target)));
+#define MORJ_REDUCE(MODE, W)                                                                                     \
+  MORJ_VPT_SWITCH(H, (st2 = launch_pdl("peer::reduce_kernel", peer::reduce_kernel<V, MODE, W>, dim3(grid),       \
+                                       dim3(ROW_THREADS), 0, s, *p, n, wa, sc, wb, eps, hn, push_x, partial_target)))
+  if (p->world <= 2) {
+    if (mode == 0) { MORJ_REDUCE(0, 2); } else { MORJ_REDUCE(1, 2); }
+  } else if (p->world <= 4) {
+    if (mode == 0) { MORJ_REDUCE(0, 4); } else { MORJ_REDUCE(1, 4); }
   } else {
-    MORJ_VPT_SWITCH(H, (st2 = launch_pdl("peer::reduce_kernel", peer::reduce_kernel<V, 1>, dim3(grid),
-                                         dim3(ROW_THREADS), 0, s, *p, n, wa, sc, wb, eps, has_next, push_x,
-                                         partial_target)));
+    if (mode == 0) { MORJ_REDUCE(0, 8); } else { MORJ_REDUCE(1, 8); }
   }
+#undef MORJ_REDUCE
   return st2;
 }
 

@@ -2,7 +2,9 @@
 (`morj_gemm_workspace_set`), the tiles of the last waves are cut along K between neighbouring SM pairs. Each
 epilogue (store, GeGLU, QKV head epilogue, tensor-parallel partial rows) against the FP32 torch reference (same
 tolerance as the other GEMM tests: max |got - ref| <= 1e-2 max |ref|) and against the same call without a
-workspace (every tile whole); two launches in a row give identical bits (the flags are back at zero)."""
+workspace (every tile whole); two launches in a row give identical bits (the flags are back at zero). With at most 16
+rows the same workspace serves the weight-streaming kernel (every tile's K range spread over all SMs), checked the
+same way against the FP32 reference and the tiled kernels."""
 import ctypes
 
 import numpy as np
@@ -176,3 +178,65 @@ def test_workspace_arguments():
     nat.call('morj_gemm_workspace_set', stream(), buf.data_ptr(), n)
     nat.call('morj_gemm_workspace_set', stream(), None, 0)                      # removed again
     nat.call('morj_gemm_workspace_remove', buf.data_ptr())                      # (nothing left to remove)
+
+
+def skinny_three(launch):
+    """(skinny, skinny again, tiled): M <= 16 with the workspace registered, twice, then the one-CTA tiled kernel
+    (forced, never the skinny path) on the same stream."""
+    ws = nat.GemmWorkspace(DEV)
+    ws.register(stream())
+    try:
+        first = launch(0)
+        second = launch(0)
+        tiled = launch(0x200)
+    finally:
+        ws.close()
+    assert nat.device_error(stream()) == 0
+    return first, second, tiled
+
+
+# the last layer's O (K 4096) and down (K 21504) shapes at 9 and 1 rows; a partial last tile (N 144) with a ragged
+# last k-block (K 4104); one unit on one CTA (128 x 64); 208 tiles of 9 k-blocks (two pieces per tile at most)
+@pytest.mark.parametrize('M,N,K', [(9, 5376, 4096), (9, 5376, 21504), (1, 5376, 4096), (16, 4096, 5376),
+                                   (9, 144, 4104), (3, 128, 64), (12, 26624, 520)])
+def test_skinny_store(M, N, K):
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+
+    def launch(force):
+        c = torch.full((M, N + 16), float('nan'), device=DEV, dtype=torch.bfloat16)  # ldc > N: the pad stays NaN
+        nat.call('morj_gemm_bf16', a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), N + 16, M, N, K,
+                 nat.EPI_STORE | force, stream())
+        torch.cuda.synchronize()
+        return c
+    first, second, tiled = skinny_three(launch)
+    assert torch.equal(first[:, :N], second[:, :N])
+    assert torch.isnan(first[:, N:].float()).all()  # (NaN: compared apart, NaN != NaN)
+    ref = a.float() @ b.float().T
+    close(first[:, :N], ref)
+    close(first[:, :N], tiled[:, :N])
+
+
+@pytest.mark.parametrize('M,F,K', [(9, 21504, 5376), (5, 384, 200), (16, 1152, 1000)])
+def test_skinny_geglu(M, F, K):
+    from morj_b200.lean_core import interleave_glu
+    from oracle.lean_oracle import gelu_tanh
+    g = torch.Generator(device=DEV).manual_seed(M + F + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    gate = (torch.randn(F, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    up = (torch.randn(F, K, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    w = interleave_glu(gate, up).contiguous()
+
+    def launch(force):
+        out = torch.empty(M, F, device=DEV, dtype=torch.bfloat16)
+        nat.call('morj_gemm_bf16', a.data_ptr(), K, w.data_ptr(), K, out.data_ptr(), F, M, 2 * F, K,
+                 nat.EPI_GEGLU | force, stream())
+        torch.cuda.synchronize()
+        return out
+    first, second, tiled = skinny_three(launch)
+    assert torch.equal(first, second)
+    gv = (a.float() @ gate.float().T).bfloat16().float()
+    uv = (a.float() @ up.float().T).bfloat16().float()
+    close(first, gelu_tanh(gv) * uv)
+    close(first, tiled)

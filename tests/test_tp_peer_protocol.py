@@ -16,7 +16,7 @@ from morj_b200.tp import BLOCK, exchange_layout, owner, partial_target, row_targ
 def test_exchange_layout(world, hidden, max_rows):
     lay = exchange_layout(world, hidden, max_rows)
     mb = lay['max_blocks']
-    assert mb * BLOCK >= max_rows
+    assert mb * BLOCK >= max_rows and mb % world == 0  # every owner's inbox holds world blocks per owned block
     regions = sorted(lay['regions'].values())
     for (o1, s1), (o2, _) in zip(regions, regions[1:]):
         assert o1 % 256 == 0 and o1 + s1 <= o2
@@ -28,7 +28,7 @@ def test_exchange_layout(world, hidden, max_rows):
 def _simulate_site(partials, rows, world, hidden, n, max_blocks, bn, rng):
     """One site, by the kernels' counting rules: `gemm_sm100.cu` epilogue_peer (every epilogue warp of every tile of
     a row block below ceil(n/128) counts that tile's columns on the owner's counter), `tp_peer.cu` reduce_kernel
-    (one CTA per 4 owned rows below ceil(n/128) * 128 counts 4 rows on every rank; the last CTA pads both counters
+    (one CTA per owned row below ceil(n/128) * 128 counts 1 row on every rank; the last CTA pads both counters
     for the blocks past n). The order of arrivals is shuffled: counters are sums."""
     n_blocks = -(-n // BLOCK)
     events = []
@@ -42,7 +42,7 @@ def _simulate_site(partials, rows, world, hidden, n, max_blocks, bn, rng):
             if owner(b, world) == r:
                 events += [('r', q, b, 128) for q in range(world)]
         for b in range(r, n_blocks, world):
-            events += [('r', q, b, 4) for q in range(world)] * 32
+            events += [('r', q, b, 1) for q in range(world)] * 128
     for i in rng.permutation(len(events)):
         kind, rank, b, v = events[i]
         (partials if kind == 'p' else rows)[rank][b] += v

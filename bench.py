@@ -215,6 +215,7 @@ def kernel_arm(args):
     attention / attention-window: the op-level paged tree attention (2048 + 8 x 64 tokens, 32/16 heads of 128, pages
     of 64 through a shuffled page table), global or sliding window 1024;
     attention-text-sliding / attention-text-global: one layer's attention of the 31B text tree on its planner tables;
+    attn-epilogue / mlp-epilogue: a residual epilogue on `--m` rows of 5376 (2040: the text tree);
     peer-reduce: one tensor-parallel site's owner reduction on the latency tree's rows, `--world` ranks emulated."""
     import torch
     from morj_b200 import _native as nat
@@ -294,6 +295,27 @@ def kernel_arm(args):
                      t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), None, len(qo) - 1, 0, hq, hk, d, 1, window,
                      1.0, t[3].data_ptr(), len(work) // 2, s)
         shape = dict(tokens=n, window=window, tiles=len(work) // 2)
+    elif args.kernel in ('attn-epilogue', 'mlp-epilogue'):
+        # the post-attention / post-MLP residual epilogue on the text tree's rows (2040 x 5376); launches cycle through
+        # four sets of rows (264 MB, past L2) so each reads its inputs from HBM
+        n, H = args.m, 5376
+        g = torch.Generator(device=dev).manual_seed(0)
+        sets = [[torch.randn(n, H, device=dev, generator=g).to(torch.bfloat16) for _ in range(3)] for _ in range(4)]
+        wn = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16)
+        sc = torch.full((1,), 0.75, device=dev).to(torch.bfloat16)
+        nbytes = 4 * n * H * 2  # o (or d) and x read, x and h written
+        turn = [0]
+
+        def launch():
+            o, x, h = sets[turn[0] % 4]
+            turn[0] += 1
+            if args.kernel == 'attn-epilogue':
+                nat.call('morj_attn_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), wn.data_ptr(), wn.data_ptr(),
+                         n, H, 1e-6, s)
+            else:
+                nat.call('morj_mlp_epilogue', o.data_ptr(), x.data_ptr(), h.data_ptr(), wn.data_ptr(), sc.data_ptr(),
+                         wn.data_ptr(), n, H, 1e-6, 1, s)
+        shape = dict(rows=n, hidden=H)
     elif args.kernel == 'peer-reduce':
         # the owner's reduction of one tensor-parallel site (post-attention epilogue) on the latency tree's rows
         # (8192 + 8 x 64, hidden 5376), the `args.world` ranks of a group emulated on this GPU: every rank's
@@ -358,7 +380,7 @@ def kernel_arm(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     pk = peaks()
-    if args.kernel == 'peer-reduce':
+    if args.kernel in ('peer-reduce', 'attn-epilogue', 'mlp-epilogue'):
         gbs = nbytes / (ms / 1000) / 1e9
         print(json.dumps(dict(kernel=args.kernel, shape=shape, ms=round(ms, 4), gbs=round(gbs, 1),
                               frac_of_copy_peak=round(gbs / pk['hbm'], 4), peak_source=pk['source'],
@@ -463,7 +485,7 @@ def main():
                     help='replicas at N > 1: skip the tensor-parallel latency leg that follows the replica measurement')
     ap.add_argument('--kernel', choices=['gemm', 'geglu', 'qkv', 'attention', 'attention-window',
                                          'attention-text-sliding', 'attention-text-global', 'peer-reduce',
-                                         'vision'],
+                                         'attn-epilogue', 'mlp-epilogue', 'vision'],
                     help='time one kernel alone instead of the tree forward')
     ap.add_argument('--no-split', action='store_true',
                     help='no split-tile workspace registered (every GEMM tile computed whole)')

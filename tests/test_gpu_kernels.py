@@ -218,10 +218,9 @@ def test_bidirectional_image_segments():
     close(got, ref, 5e-2)
 
 
-@pytest.mark.parametrize('H', [256, 5376])
-def test_row_epilogues_match_oracle(H):
+@pytest.mark.parametrize('H,n', [(256, 67), (5376, 67), (5376, 2040), (8192, 67)])
+def test_row_epilogues_match_oracle(H, n):
     from oracle.lean_oracle import attn_epilogue, mlp_epilogue, rmsnorm
-    n = 67
     o = torch.randn(n, H).to(torch.bfloat16)
     x = (torch.randn(n, H) * 3).to(torch.bfloat16)
     wp, wq, wn = [(1 + 0.1 * torch.randn(H)).to(torch.bfloat16) for _ in range(3)]
@@ -242,6 +241,12 @@ def test_row_epilogues_match_oracle(H):
     xr2, hr2 = mlp_epilogue(o, x, wp, sc, wn, 1e-6)
     close(xd2, xr2)
     close(h, hr2)
+    # the last layer's form: no next layer, x written in place, h untouched
+    xd3, h_keep = x.to(DEV).clone(), h.clone()
+    nat.call('morj_mlp_epilogue', od.data_ptr(), xd3.data_ptr(), h.data_ptr(), wp_d.data_ptr(), sc_d.data_ptr(),
+             None, n, H, 1e-6, 0, stream())
+    torch.cuda.synchronize()
+    assert torch.equal(xd3, xd2) and torch.equal(h, h_keep)
     # embedding + image feature rows + input norm
     V = 1000
     emb = (torch.randn(V, H) * 0.02).to(torch.bfloat16)

@@ -60,7 +60,7 @@ def test_two_gpu_tensor_parallel_matches_reference():
     if torch.cuda.device_count() < 2:
         pytest.skip('needs 2 GPUs')
     world = 2
-    out = mp.Manager().dict()
+    out = mp.get_context('spawn').Manager().dict()
     mp.start_processes(_rank, args=(world, _port(), out), nprocs=world, join=True, start_method='spawn')
     with open(GOLDEN) as f:
         cases = {c['name']: c for c in json.load(f)['cases']}

@@ -68,16 +68,15 @@ def test_tensor_parallel_on_every_gpu_matches_one_gpu():
     if world < 2:
         pytest.skip('needs 2 or more GPUs')
     world = 8 if world >= 8 else 4 if world >= 4 else 2
+    # the ranks first (spawned, before this process touches CUDA), then the one-GPU run here
+    out = mp.get_context('spawn').Manager().dict()
+    mp.start_processes(_rank, args=(world, _port(), out), nprocs=world, join=True, start_method='spawn')
     from morj_b200.checkpoint import random_state
     from morj_b200.lean_core import LeanGemma4
     top = config()
     seqs, labels = request()
     one = LeanGemma4.from_state(top, random_state(top, seed=5), device='cuda:0')
     want = np.concatenate(one.run(one.prepare(seqs, labels), list(range(len(seqs)))))
-    del one
-    torch.cuda.empty_cache()
-    out = mp.Manager().dict()
-    mp.start_processes(_rank, args=(world, _port(), out), nprocs=world, join=True, start_method='spawn')
     for key, got in out[0].items():
         err = np.abs(got - want).max()
         print(f'\n{world} ranks {key}: max |TP - one GPU| = {err:.2e}')

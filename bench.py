@@ -132,8 +132,8 @@ def bench_config(args, world, desc, tokens, flops):
     """The `config` object of the JSON line; both arms print the same one for the same arguments."""
     tp = args.mode == 'tp' and world > 1
     par = (f'replicas x{world} (independent trees, no collective)' if not tp else
-           f'tensor parallel x{world} (O/down partial rows stored by the GEMMs into their row owners\' memory over '
-           f'NVLink, reduced with the epilogues)' if args.tp_comm == 'peer' else f'tensor parallel x{world} (NCCL all-reduce after O and down)')
+           f'tensor parallel x{world} (O/down partial rows read by their row owners over NVLink, reduced with the '
+           f'epilogues)' if args.tp_comm == 'peer' else f'tensor parallel x{world} (NCCL all-reduce after O and down)')
     work = (f'31B-class Gemma-style decoder, {desc}' if not args.layers else
             f'31B-class Gemma-style decoder cut to {args.layers} layers (profiling), {desc}')
     return dict(workload=work, tokens=tokens, parallelism=par,
@@ -319,8 +319,8 @@ def kernel_arm(args):
     elif args.kernel == 'peer-reduce':
         # the owner's reduction of one tensor-parallel site (post-attention epilogue) on the latency tree's rows
         # (8192 + 8 x 64, hidden 5376), the `args.world` ranks of a group emulated on this GPU: every rank's
-        # row-parallel GEMM has delivered its partials into the owners' inboxes once, so the timed launches of rank
-        # 0's reduction find their counters met and read and write this GPU's memory only
+        # row-parallel GEMM has written its partials once, so the timed launches of rank 0's reduction find their
+        # counters met and read and write this GPU's memory only (no NVLink: the kernel's own cost)
         import ctypes
         from morj_b200.tp import exchange_layout, owner, partial_target
         world, n, H, k = args.world, 8704, 5376, 64
@@ -711,14 +711,15 @@ def main():
                           launches=len(big), avg_launch_us=round(1000 * g_ms / max(len(big), 1), 2),
                           all_gemms_tflops=round(all_tf, 1),
                           attention=dict(achieved=round(flops_attn / (attn_ms / 1000) / 1e12, 1) if attn_ms else None,
-                                         peak=pk['bf16'], frac=round(flops_attn / (attn_ms / 1000) / 1e12 / pk['bf16'],
-                                                                     4) if attn_ms else None,
+                                         peak=pk['bf16_sustained'],
+                                         frac=round(flops_attn / (attn_ms / 1000) / 1e12 / pk['bf16_sustained'], 4)
+                                         if attn_ms else None,
                                          unit='TFLOP/s', ms_per_tree=round(attn_ms, 3),
                                          tflop_per_tree=round(flops_attn / 1e12, 3),
                                          basis='algorithmic FLOPs (4 x Hq x d per visible pair, all layers as '
                                                'specified) / summed attention launch times of one traced tree (an '
-                                               'event pair around every launch: launch gaps included); peak: '
-                                               'burst cuBLAS BF16',
+                                               'event pair around every launch); peak: sustained cuBLAS BF16 '
+                                               '(kernels timed inside a step run at its power-capped clock)',
                                          back_to_back=alone)),
             breakdown_ms={k: round(v['ms'], 3) for k, v in per_kind.items()},
             breakdown_basis=('one traced tree: a CUDA event pair around every launch, the whole tree queued behind a '

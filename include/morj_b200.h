@@ -177,10 +177,9 @@ int morj_geglu(const void* gu, int n, int F, void* out, void* stream);
  * replaces the NCCL all-reduce after the row-parallel O and down projections of a T-way sharded model) ----------
  *
  * Rows are owned in blocks of 128: row block b belongs to rank b % world. Each rank's row-parallel GEMM stores its
- * BF16 partial rows of block b straight into the owner's `part` buffer (its inbox; NVLink stores for a peer), at
- * inbox block (b - b % world) + rank, and counts the columns it wrote on the owner's per-block counter (an atomic in
- * the owner's memory); the owner's reduce kernel waits for all ranks' columns, reads the partial rows of its blocks
- * from its own inbox (local HBM), sums them in rank order in FP32, rounds to BF16 (the
+ * BF16 partial rows in its own `part` buffer and counts the columns it wrote on the owner's per-block counter (an
+ * atomic in the owner's memory); the owner's reduce kernel waits for all ranks' columns, reads the partial rows of
+ * its blocks from every rank (NVLink loads from peer memory), sums them in rank order in FP32, rounds to BF16 (the
  * value an NCCL BF16 all-reduce gives for two ranks), applies the post-attention or post-MLP epilogue to its own
  * rows, and stores the new h rows (and, when asked, x rows) into every rank's buffers, counting rows on their
  * per-block counters. A wait kernel then holds the stream until every row block of h has arrived. Counters only
@@ -192,9 +191,9 @@ int morj_geglu(const void* gu, int n, int F, void* out, void* stream);
 typedef struct morj_peer {
   int world;       /* ranks (1..8) */
   int rank;        /* this rank */
-  int max_blocks;  /* row blocks of 128 each buffer holds; a multiple of world */
+  int max_blocks;  /* row blocks of 128 each buffer holds */
   int hidden;      /* H, columns of every exchanged row */
-  void* part[MORJ_MAX_RANKS];                  /* rank r's inbox of partial rows, [max_blocks * 128, H] BF16 */
+  void* part[MORJ_MAX_RANKS];                  /* rank r's partial rows, [max_blocks * 128, H] BF16 */
   void* x[MORJ_MAX_RANKS];                     /* rank r's residual rows, [max_blocks * 128, H] BF16 */
   void* h[MORJ_MAX_RANKS];                     /* rank r's normed rows, [max_blocks * 128, H] BF16 */
   unsigned long long* partials[MORJ_MAX_RANKS]; /* rank r's partial-column counters, [max_blocks] */
@@ -209,8 +208,8 @@ int morj_ipc_export(const void* ptr, void* handle);
 int morj_ipc_import(const void* handle, void** ptr);
 int morj_ipc_close(void* ptr, const void* handle);
 
-/* Row-parallel GEMM: its BF16 partial rows C = A . B^T ([M, N], N = hidden, M <= max_blocks * 128) go to their
- * row block owners' inboxes, each tile counted on the owner's counter; the kernel is chosen per shape as for
+/* Row-parallel GEMM: its BF16 partial rows C = A . B^T ([M, N], N = hidden, M <= max_blocks * 128) go to this
+ * rank's part buffer, each tile counted on its row block owner's counter; the kernel is chosen per shape as for
  * morj_gemm_bf16. */
 int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                         const morj_peer_t* peer, void* stream);

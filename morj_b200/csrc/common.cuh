@@ -357,6 +357,19 @@ MORJ_DEV float block_sum(float v, float* red) {
   return t;
 }
 
+// block_sum into a `red` array that no earlier reduction of this CTA has used: one barrier instead of two (a CTA
+// that reduces twice per row gives each reduction its own array)
+MORJ_DEV float block_sum_fresh(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x / 32;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
 MORJ_DEV void load8(const __nv_bfloat16* p, float (&v)[8]) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);

@@ -55,16 +55,16 @@ struct QkvEpi {
   __nv_bfloat16* v_pool;
 };
 
-// Operands of the partial epilogue (tensor parallelism over peer memory): the output rows of row block b go
-// straight into the inbox of its owner, rank b % world (its part buffer, over NVLink for a peer), at inbox block
-// (b - b % world) + rank, and the columns written are counted on the owner's counter b. The owner's reduction then
-// reads every rank's partial from its own HBM, and the NVLink transfer overlaps the GEMM's later tiles.
+// Operands of the partial epilogue (tensor parallelism over peer memory): the output rows go to this rank's part
+// buffer and the columns written for row block b are counted on the counter b of its owner, rank b % world. (Storing
+// the rows straight into the owner's memory instead, so that NVLink would carry them while later tiles compute,
+// measured slower: at 4 ranks the row-parallel GEMMs took 68 instead of 30 ms per latency tree, the epilogue warps'
+// remote stores and system fences holding the accumulators, for a 13 ms saving in the reduction.)
 constexpr int EPI_PEER = 4;
 struct PeerEpi {
-  __nv_bfloat16* part[MORJ_MAX_RANKS];
+  __nv_bfloat16* part;
   unsigned long long* partials[MORJ_MAX_RANKS];
   int world;
-  int rank;
 };
 
 // Split tiles of the pair kernel. When the tiles do not fill whole waves of SM pairs, the tiles of the last one to
@@ -358,18 +358,16 @@ MORJ_DEV void store_row(uint32_t tacc, __nv_bfloat16* crow, int n_blk, bool row_
   }
 }
 
-// Partial epilogue: this thread's row of the tile goes to the row block owner's inbox (the STORE epilogue's stores);
-// the tile's column count for the owner is returned, to be posted by `peer_arrive`. Row blocks wholly past M (the
-// pair kernel's padding) neither store nor count.
+// Partial epilogue: this thread's row of the tile goes to this rank's part buffer (the STORE epilogue's stores);
+// the tile's column count for the row block's owner is returned, to be posted by `peer_arrive`. Row blocks wholly
+// past M (the pair kernel's padding) neither store nor count.
 template <int BN>
 MORJ_DEV void epilogue_peer(uint32_t tacc, int row, int n_blk, int M, int N, const PeerEpi& pe,
                             unsigned long long*& count, unsigned long long& cols) {
   const int blk = row / 128;
   if (blk * 128 >= M) return;
-  const int own = blk % pe.world;
-  const size_t slot = (size_t)(blk - own + pe.rank) * 128 + (row & 127);
-  store_row<BN>(tacc, pe.part[own] + slot * N, n_blk, row < M, N);
-  count = pe.partials[own] + blk;
+  store_row<BN>(tacc, pe.part + (size_t)row * N, n_blk, row < M, N);
+  count = pe.partials[blk % pe.world] + blk;
   cols = (unsigned long long)(min(N, (n_blk + 1) * BN) - n_blk * BN);
 }
 
@@ -1036,12 +1034,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 // ---------------------------------------------------------------------------------------------------------------
 // Skinny kernel, M <= 16 activation rows (the last layer's readout rows): C = X . W^T is computed as W . X^T, so the
 // weights are the MMA's A operand (128 weight rows per tile, M = 128) and stream through the SMs once, and the
-// activation rows are its B operand (N = 16; rows past M are zero-filled by TMA). The (tile, k-block) units, tile-major,
-// are cut into one contiguous range per CTA, one CTA per SM, so every SM streams the same number of weight bytes
-// whatever the tile count (the 42 tiles of a 5376-wide projection would leave 106 of 148 SMs idle). A range's piece of
-// a tile accumulates in TMEM and goes to the workspace as an FP32 [128 x 16] partial; the piece that completes a tile
-// (an atomic count per tile, or per gate/up tile pair with the GeGLU epilogue) adds the tile's pieces in k order
-// (so the sum does not depend on arrival order), rounds, and stores the output columns of the M rows.
+// activation rows are its B operand (N = 16; rows past M are zero-filled by TMA). The (tile, k-block) units,
+// tile-major, are cut into one contiguous range per CTA, one CTA per SM, so every SM streams the same number of
+// weight bytes whatever the tile count (the 42 tiles of a 5376-wide projection would leave 106 of 148 SMs idle). A
+// range's piece of a tile accumulates in TMEM and goes to the workspace as an FP32 [128 x 16] partial; the piece that
+// completes a tile (an atomic count per tile, or per gate/up tile pair with the GeGLU epilogue) adds the tile's
+// pieces in k order (so the sum does not depend on arrival order), rounds, and stores the output columns of the M
+// rows.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int SK_N = 16;
 constexpr int SK_B_BYTES = SK_N * BK * 2;
@@ -1229,8 +1228,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         acc_phase ^= 1;
       }
       const int first = sk_owner((long long)t * kb, ctas, units);
-      float4* slot = reinterpret_cast<float4*>(sk.slots + ((size_t)t * sk.pmax + (blockIdx.x - first)) * SK_SLOT_FLOATS +
-                                               r * SK_N);
+      float4* slot = reinterpret_cast<float4*>(
+          sk.slots + ((size_t)t * sk.pmax + (blockIdx.x - first)) * SK_SLOT_FLOATS + r * SK_N);
 #pragma unroll
       for (int q = 0; q < SK_N / 4; ++q)
         slot[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
@@ -1558,7 +1557,7 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
   if (!A || !B || !peer || M < 0 || N <= 0 || K <= 0)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: bad pointers or sizes (M=%d N=%d K=%d)", M, N, K);
   if (peer->world < 1 || peer->world > MORJ_MAX_RANKS || peer->rank < 0 || peer->rank >= peer->world ||
-      peer->max_blocks % peer->world || N != peer->hidden || M > peer->max_blocks * 128)
+      N != peer->hidden || M > peer->max_blocks * 128)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: exchange buffers do not fit (M=%d N=%d)", M, N);
   if (N % 16 || K % 8 || lda % 8 || ldb % 8 || lda < K || ldb < K)
     return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: N % 16, K and leading dimensions % 8 required");
@@ -1568,13 +1567,12 @@ extern "C" int morj_gemm_bf16_peer(const void* A, long long lda, const void* B, 
   for (int r = 0; r < peer->world; ++r) {
     if (!peer->partials[r] || (reinterpret_cast<uintptr_t>(peer->partials[r]) & 7))
       return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's counters are missing or unaligned", r);
-    if (!peer->part[r] || (reinterpret_cast<uintptr_t>(peer->part[r]) & 15))
-      return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: rank %d's part buffer is missing or unaligned", r);
     pe.partials[r] = peer->partials[r];
-    pe.part[r] = reinterpret_cast<__nv_bfloat16*>(peer->part[r]);
   }
+  if (!peer->part[peer->rank] || (reinterpret_cast<uintptr_t>(peer->part[peer->rank]) & 15))
+    return set_error(MORJ_ERR_ARG, "morj_gemm_bf16_peer: part buffer missing or unaligned");
+  pe.part = reinterpret_cast<__nv_bfloat16*>(peer->part[peer->rank]);
   pe.world = peer->world;
-  pe.rank = peer->rank;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   static const int cand[] = {256, 208, 192, 128};
   // (the widths the STORE path picks for these shapes)

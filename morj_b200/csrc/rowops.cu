@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(THREADS) embed_rmsnorm_kernel(const int* __res
       store8(x_out + row * H + c, v[k]);
     }
   }
-  const float inv = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
+  const float inv = 1.0f / sqrtf(block_sum_fresh(ss, red) / H + eps);
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
                                                                 float eps) {
   pdl_wait();  // the previous kernel on the stream has completed
   pdl_trigger();
-  __shared__ float red[32];
+  __shared__ float red[2][32];  // one array per reduction
   const size_t base = (size_t)blockIdx.x * H;
   uint4 o_raw[VPT], x_raw[VPT], w_raw[VPT];
 #pragma unroll
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
       for (int e = 0; e < 8; ++e) ss += ov[e] * ov[e];
     }
   }
-  const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
+  const float inv1 = 1.0f / sqrtf(block_sum_fresh(ss, red[0]) / H + eps);
   float ss2 = 0.f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(THREADS) attn_epilogue_kernel(const __nv_bfloa
       w_raw[k] = *reinterpret_cast<const uint4*>(w_pre + c);
     }
   }
-  const float inv2 = 1.0f / sqrtf(block_sum(ss2, red) / H + eps);
+  const float inv2 = 1.0f / sqrtf(block_sum_fresh(ss2, red[1]) / H + eps);
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
                                                                float eps, int has_next) {
   pdl_wait();  // the previous kernel on the stream has completed
   pdl_trigger();
-  __shared__ float red[32];
+  __shared__ float red[2][32];  // one array per reduction
   const size_t base = (size_t)blockIdx.x * H;
   const float sc = __bfloat162float(scalar[0]);
   uint4 d_raw[VPT], x_raw[VPT], w_raw[VPT];
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
       for (int e = 0; e < 8; ++e) ss += dv[e] * dv[e];
     }
   }
-  const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
+  const float inv1 = 1.0f / sqrtf(block_sum_fresh(ss, red[0]) / H + eps);
   float ss2 = 0.f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(THREADS) mlp_epilogue_kernel(const __nv_bfloat
     }
   }
   if (!has_next) return;
-  const float inv2 = 1.0f / sqrtf(block_sum(ss2, red) / H + eps);
+  const float inv2 = 1.0f / sqrtf(block_sum_fresh(ss2, red[1]) / H + eps);
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = (threadIdx.x + k * THREADS) * 8;

@@ -2,12 +2,12 @@
 // hand-back of the reduced rows, replacing an NCCL all-reduce followed by replicated epilogues.
 //
 // Row block b (128 rows) belongs to rank b % world. Every rank's row-parallel GEMM (morj_gemm_bf16_peer) has stored
-// its BF16 partial rows of block b into the owner's part buffer (its inbox, at block (b - b % world) + source rank)
-// and counted the columns on the owner's counter. Here the owner
+// its BF16 partial rows in its own part buffer and counted the columns of block b on the owner's counter. Here the
+// owner
 //   1. waits (one thread per CTA, acquire at system scope, bounded) until block b's counter holds every rank's
 //      columns for this site,
-//   2. reads block b's partial rows of every rank from its own inbox (local HBM), sums them in rank order in FP32
-//      and rounds to BF16,
+//   2. reads block b's partial rows from every rank (NVLink loads from the peers' part buffers), sums them in rank
+//      order in FP32 and rounds to BF16,
 //   3. applies the post-attention or post-MLP epilogue (the math of morj_attn_epilogue / morj_mlp_epilogue) to its
 //      rows, and
 //   4. stores the new h rows (and x rows, when asked) into every rank's buffers over NVLink, then counts one row on
@@ -53,9 +53,9 @@ MORJ_DEV bool wait_at_least(const unsigned long long* p, unsigned long long targ
 // partials right after it, as packed BF16, two ranks at a time with the loop over ranks unrolled to W (the group
 // size rounded up to 2, 4 or 8): a runtime loop over ranks left one load round trip per rank and vector in the
 // chain, and holding all W partials at once cut the CTAs per SM to one at W = 8. The partials go through L2 only
-// (`ld.cg`): peers' GEMMs write them while this kernel runs. The row's stores are published by one barrier and the
-// release atomics that count the row (release is cumulative over the barrier, as in a stream-K fix-up's arrival);
-// a system fence in every thread stalled the kernel most of its time.
+// (`ld.cg`): the peers' GEMMs write them while this kernel may run. The row's stores are published by one barrier
+// and the release atomics that count the row (release is cumulative over the barrier, as in a stream-K fix-up's
+// arrival); a system fence in every thread stalled the kernel most of its time.
 template <int VPT, int MODE, int W>
 __global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
     reduce_kernel(const morj_peer_t p, int n, const __nv_bfloat16* __restrict__ w_a,
@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
                   int has_next, int push_x, unsigned long long partial_target) {
   pdl_wait();  // the previous kernel on the stream has completed
   pdl_trigger();
-  __shared__ float red[32];
+  __shared__ float red[2][32];  // one array per reduction
   __shared__ int ok_s;
   const int H = p.hidden, world = p.world, rank = p.rank;
   const int n_blocks = (n + 127) / 128;
@@ -93,9 +93,6 @@ __global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
   __syncthreads();
   if (!ok_s) return;  // the peers' waits for this block's rows run out and report too
   if (live) {
-    // source rank s's partial of this row: inbox block blk - rank + s, the row's offset in the block
-    const __nv_bfloat16* in =
-        reinterpret_cast<const __nv_bfloat16*>(p.part[rank]) + ((size_t)(blk - rank) * 128 + (row & 127)) * H;
     float ov[VPT][8];
 #pragma unroll
     for (int s0 = 0; s0 < W; s0 += 2) {
@@ -107,7 +104,8 @@ __global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
 #pragma unroll
           for (int j = 0; j < 2; ++j)
             if (s0 + j < world)
-              raw[j][k] = __ldcg(reinterpret_cast<const uint4*>(in + (size_t)(s0 + j) * 128 * H + c));
+              raw[j][k] = __ldcg(reinterpret_cast<const uint4*>(
+                  reinterpret_cast<const __nv_bfloat16*>(p.part[s0 + j]) + (size_t)row * H + c));
         }
       }
 #pragma unroll
@@ -139,7 +137,7 @@ __global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
       }
     }
     const float sc = MODE == 1 ? __bfloat162float(scalar[0]) : 1.f;
-    const float inv1 = 1.0f / sqrtf(block_sum(ss, red) / H + eps);
+    const float inv1 = 1.0f / sqrtf(block_sum_fresh(ss, red[0]) / H + eps);
     float ss2 = 0.f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
@@ -162,7 +160,7 @@ __global__ void __launch_bounds__(ROW_THREADS, W == 2 ? 4 : 3)
       }
     }
     if (MODE == 0 || has_next) {
-      const float inv2 = 1.0f / sqrtf(block_sum(ss2, red) / H + eps);
+      const float inv2 = 1.0f / sqrtf(block_sum_fresh(ss2, red[1]) / H + eps);
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         const int c = (threadIdx.x + k * ROW_THREADS) * 8;
@@ -192,7 +190,7 @@ __global__ void __launch_bounds__(ROW_THREADS) wait_kernel(const unsigned long l
 
 static int check_peer(const morj_peer_t* p, const char* who) {
   if (!p || p->world < 1 || p->world > MORJ_MAX_RANKS || p->rank < 0 || p->rank >= p->world || p->max_blocks <= 0 ||
-      p->max_blocks % p->world || p->hidden <= 0 || p->hidden % 8)
+      p->hidden <= 0 || p->hidden % 8)
     return set_error(MORJ_ERR_ARG, "%s: bad exchange description", who);
   for (int r = 0; r < p->world; ++r)
     if (!p->part[r] || !p->x[r] || !p->h[r] || !p->partials[r] || !p->rows[r] ||

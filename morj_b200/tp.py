@@ -75,12 +75,10 @@ BLOCK = 128
 
 
 def exchange_layout(world, hidden, max_rows):
-    """Byte layout of one rank's exchange allocation: its inbox of partial rows of a row-parallel projection (every
-    rank's partial of each row block this rank owns, written there by the ranks' GEMMs: source rank s of block b at
-    inbox block b - b % world + s), the x and h rows of a whole step, and the two per-block counter arrays. The
-    block count is a multiple of `world`; every region starts on a 256-byte boundary."""
+    """Byte layout of one rank's exchange allocation: its partial rows of a row-parallel projection (read by the row
+    blocks' owners), the x and h rows of a whole step, and the two per-block counter arrays. Every region starts on
+    a 256-byte boundary."""
     max_blocks = max(1, -(-max_rows // BLOCK))
-    max_blocks = -(-max_blocks // world) * world
     rows = max_blocks * BLOCK * hidden * 2
     sizes = dict(part=rows, x=rows, h=rows, partials=max_blocks * 8, rows=max_blocks * 8)
     off, layout = 0, {}

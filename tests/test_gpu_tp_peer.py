@@ -42,17 +42,8 @@ class Group:
         return self.bufs[r][off:off + rows * self.hidden * 2].view(torch.bfloat16).view(rows, self.hidden)
 
     def delivered(self, n):
-        """Every rank's partial rows [0, n): [world, n, hidden], gathered from the owners' inboxes (source rank s of
-        row block b at block b - b % world + s of owner b % world's part buffer)."""
-        nb = -(-n // BLOCK)
-        inbox = [self.region(r, 'part', self.lay['max_blocks'] * BLOCK) for r in range(self.world)]
-        out = torch.empty(self.world, nb * BLOCK, self.hidden, dtype=torch.bfloat16, device=DEV)
-        for b in range(nb):
-            own = owner(b, self.world)
-            for s in range(self.world):
-                slot = b - own + s
-                out[s, b * BLOCK:(b + 1) * BLOCK] = inbox[own][slot * BLOCK:(slot + 1) * BLOCK]
-        return out[:, :n]
+        """Every rank's partial rows [0, n): [world, n, hidden], read from their part buffers."""
+        return torch.stack([self.region(r, 'part', n) for r in range(self.world)])
 
     def site(self, a, w, mode, n, w_a, scalar, w_b, has_next, push_x):
         s = stream()

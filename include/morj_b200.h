@@ -91,6 +91,13 @@ int morj_gemm_workspace_remove(const void* ptr);
  * then the epilogue). Returns the number of items, -1 on bad arguments or when cap is too small. */
 int morj_gemm_split_walk(int tiles, int pairs, int kblocks, int pair, int* items, int cap);
 
+/* The schedule of the weight-streaming kernel morj_gemm_bf16 runs for M <= 16 rows (host function, no device
+ * access): the (tile, k-block) units of `tiles` tiles of `kblocks` k-blocks, tile-major, cut into `ctas` contiguous
+ * ranges; CTA `cta` walks, in order, (tile, first k-block, end k-block, piece, pieces) int quintuples: its piece of
+ * each tile it touches and the tile's piece count. Returns the number of items, -1 on bad arguments (ctas must not
+ * exceed tiles x kblocks) or when cap is too small. */
+int morj_gemm_skinny_walk(int tiles, int kblocks, int ctas, int cta, int* items, int cap);
+
 /* The QKV projection with the head epilogue fused: [q | k | v] = A . W^T (W: [N, K] rows q heads, k heads, v heads if
  * has_v; N = (hq + (1 + has_v) * hk) * d), each head RMSNorm'ed over the BF16-rounded projection (q, k weighted;
  * v unweighted), rounded, RoPE'd (q, k) and written straight to q_out[row, hq, d] and pool row slots[row] of

@@ -32,6 +32,7 @@ SIGNATURES = {
     'morj_gemm_workspace_set': [P, P, ctypes.c_ulonglong],
     'morj_gemm_workspace_remove': [P],
     'morj_gemm_split_walk': [I, I, I, I, IP, I],
+    'morj_gemm_skinny_walk': [I, I, I, I, IP, I],
     'morj_gemm_qkv_rope': [P, LL, P, LL, I, I, I, I, I, I, P, P, P, P, I, P, F, P, P, P, P],
     'morj_rope_table': [P, I, I, P, P],
     'morj_embed_rmsnorm': [P, P, P, P, I, I, F, P, F, P, P, P],
@@ -161,6 +162,18 @@ def split_walk(tiles, pairs, kblocks, pair):
     if n < 0:
         check(ERR_ARG, 'morj_gemm_split_walk')
     return buf[:4 * n].reshape(n, 4)
+
+
+def skinny_walk(tiles, kblocks, ctas, cta):
+    """The weight-streaming kernel's work for CTA `cta` of `ctas`: an [n, 5] int32 array of (tile, first k-block,
+    end k-block, piece, pieces)."""
+    import numpy as np
+    cap = tiles * kblocks // ctas + 3
+    buf = np.zeros(5 * cap, dtype=np.int32)
+    n = lib().morj_gemm_skinny_walk(tiles, kblocks, ctas, cta, buf.ctypes.data_as(IP), cap)
+    if n < 0:
+        check(ERR_ARG, 'morj_gemm_skinny_walk')
+    return buf[:5 * n].reshape(n, 5)
 
 
 class GemmWorkspace:

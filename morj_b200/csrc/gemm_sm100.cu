@@ -1064,6 +1064,17 @@ __host__ __device__ inline int sk_owner(long long u, int ctas, long long units) 
 __host__ __device__ inline int sk_pieces(int t, int kb, int ctas, long long units) {
   return sk_owner((long long)t * kb + kb - 1, ctas, units) - sk_owner((long long)t * kb, ctas, units) + 1;
 }
+// CTA `cta`'s range of units [lo, hi) (non-empty: ctas <= units), its tiles [t_first, t_last] and each tile's
+// k-blocks [k0(t), k1(t)); the piece it computes of tile t is cta - sk_owner(t * kb).
+struct SkRange {
+  long long lo, hi;
+  int kb, t_first, t_last;
+  __host__ __device__ SkRange(int cta, int ctas, int tiles, int kb_)
+      : lo((long long)tiles * kb_ * cta / ctas), hi((long long)tiles * kb_ * (cta + 1) / ctas), kb(kb_),
+        t_first((int)(lo / kb_)), t_last((int)((hi - 1) / kb_)) {}
+  __host__ __device__ int k0(int t) const { return (int)(lo > (long long)t * kb ? lo - (long long)t * kb : 0); }
+  __host__ __device__ int k1(int t) const { return (int)(hi < (long long)(t + 1) * kb ? hi - (long long)t * kb : kb); }
+};
 
 MORJ_DEV void sk_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }  // the four epilogue warps
 
@@ -1130,8 +1141,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tiles = (N + BM - 1) / BM, kb = (K + BK - 1) / BK;
   const long long units = (long long)tiles * kb;
   const int ctas = (int)gridDim.x;
-  const long long lo = units * blockIdx.x / ctas, hi = units * (blockIdx.x + 1) / ctas;  // lo < hi: ctas <= units
-  const int t_first = (int)(lo / kb), t_last = (int)((hi - 1) / kb);
+  const SkRange range((int)blockIdx.x, ctas, tiles, kb);
+  const int t_first = range.t_first, t_last = range.t_last;
   const uint32_t smem_base = smem_u32(smem);
 
   if (warp == 0) {
@@ -1142,8 +1153,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = t_first; t <= t_last && ok && !*abort; ++t) {
-        const int k0 = (int)(lo > (long long)t * kb ? lo - (long long)t * kb : 0);
-        const int k1 = (int)(hi < (long long)(t + 1) * kb ? hi - (long long)t * kb : kb);
+        const int k0 = range.k0(t), k1 = range.k1(t);
         for (int k = k0; k < k1; ++k) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kErrTimeoutGemmProducer)) {
             ok = false;
@@ -1174,8 +1184,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int t = t_first; t <= t_last && ok; ++t) {
-        const int k0 = (int)(lo > (long long)t * kb ? lo - (long long)t * kb : 0);
-        const int k1 = (int)(hi < (long long)(t + 1) * kb ? hi - (long long)t * kb : kb);
+        const int k0 = range.k0(t), k1 = range.k1(t);
         if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kErrTimeoutGemmMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * SK_N;
@@ -1690,6 +1699,26 @@ extern "C" int morj_gemm_workspace_remove(const void* ptr) {
       ++i;
   }
   return MORJ_OK;
+}
+
+extern "C" int morj_gemm_skinny_walk(int tiles, int kblocks, int ctas, int cta, int* items, int cap) {
+  using namespace morj::gemm;
+  if (tiles < 1 || kblocks < 1 || ctas < 1 || (long long)ctas > (long long)tiles * kblocks || cta < 0 ||
+      cta >= ctas || cap < 0 || (cap && !items))
+    return -1;
+  const long long units = (long long)tiles * kblocks;
+  const SkRange range(cta, ctas, tiles, kblocks);
+  int n = 0;
+  for (int t = range.t_first; t <= range.t_last; ++t) {
+    if (n == cap) return -1;
+    items[5 * n] = t;
+    items[5 * n + 1] = range.k0(t);
+    items[5 * n + 2] = range.k1(t);
+    items[5 * n + 3] = cta - sk_owner((long long)t * kblocks, ctas, units);
+    items[5 * n + 4] = sk_pieces(t, kblocks, ctas, units);
+    ++n;
+  }
+  return n;
 }
 
 extern "C" int morj_gemm_split_walk(int tiles, int pairs, int kblocks, int pair, int* items, int cap) {

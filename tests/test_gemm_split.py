@@ -61,3 +61,40 @@ def test_bad_arguments():
         nat.split_walk(10, 4, 0, 0)
     with pytest.raises(ValueError):
         nat.split_walk(10, 4, 5, 4)
+
+
+@pytest.mark.parametrize('tiles,kb,ctas', [
+    (42, 336, 148),    # 9 x 5376 x 21504 (the last layer's down projection)
+    (42, 64, 148),     # 9 x 5376 x 4096 (O)
+    (336, 84, 148),    # 9 x 43008 x 5376 (gate / up)
+    (2, 65, 130), (1, 1, 1), (208, 9, 148), (5, 3, 15), (3, 1000, 7), (148, 1, 148),
+])
+def test_skinny_schedule_covers_every_k_block_once(tiles, kb, ctas):
+    """`morj_gemm_skinny_walk` (the weight-streaming kernel's schedule, same host/device code): every k-block of every
+    tile once; a tile's pieces are consecutive CTAs in k order, numbered 0.. on each and counted the same by all; the
+    CTAs' k-block counts differ by at most one."""
+    cover = np.zeros((tiles, kb), dtype=np.int32)
+    pieces = {}
+    per_cta = []
+    for c in range(ctas):
+        items = nat.skinny_walk(tiles, kb, ctas, c)
+        assert len(items) >= 1
+        per_cta.append(int(sum(k1 - k0 for _, k0, k1, _, _ in items)))
+        for t, k0, k1, piece, n in items:
+            assert 0 <= k0 < k1 <= kb
+            cover[t, k0:k1] += 1
+            pieces.setdefault(t, []).append((k0, c, piece, n))
+    assert (cover == 1).all()
+    assert max(per_cta) - min(per_cta) <= 1
+    for t, ps in pieces.items():
+        ps.sort()
+        assert [p for _, _, p, _ in ps] == list(range(len(ps)))
+        assert all(n == len(ps) for _, _, _, n in ps)
+        assert [c for _, c, _, _ in ps] == list(range(ps[0][1], ps[0][1] + len(ps)))
+
+
+def test_skinny_walk_rejects_bad_arguments():
+    with pytest.raises(ValueError):
+        nat.skinny_walk(2, 3, 7, 0)  # more CTAs than units
+    with pytest.raises(ValueError):
+        nat.skinny_walk(2, 3, 3, 3)  # no such CTA

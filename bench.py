@@ -838,6 +838,10 @@ def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):
         barrier()
         ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
         got = np.concatenate(model.run(model.prepare(tree_in['seqs'], tree_in['label_ids']), seqs))
+        # the bench's text tree on the sharded model, for the oracle record of the same weights and tree
+        text = w.text_tree(seed=0)
+        got_text = np.concatenate(model.run(model.prepare(text['seqs'], text['label_ids']),
+                                            list(range(len(text['seqs'])))))
         model.trace = []
         model.execute_pass(p)
         torch.cuda.synchronize()
@@ -849,6 +853,18 @@ def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):
     del model
     if rank != 0:
         return None
+    parity = None
+    gfile = os.path.join(ROOT, 'tests', 'golden', 'oracle_31b_text.json')
+    if os.path.exists(gfile):
+        with open(gfile) as f:
+            rec = json.load(f)
+        bf = np.concatenate([np.asarray(r, np.float64) for r in rec['probs']])
+        fp = np.concatenate([np.asarray(r, np.float64) for r in rec['probs_fp32']])
+        parity = dict(vs='text tree on the sharded model against the oracle record of the same weights and tree '
+                         '(the one-GPU line\'s parity criterion)',
+                      max_abs_vs_bf16_path=float(np.abs(got_text - bf).max()),
+                      max_abs_vs_fp32=float(np.abs(got_text - fp).max()),
+                      bf16_path_max_abs_vs_fp32=float(np.abs(bf - fp).max()), probabilities=int(len(got_text)))
     return dict(gpus=world, workload='latency tree: 8192-token prefix + 8 branches x 64 tokens (seed 0, every rank)',
                 exchange='peer memory over NVLink: row-parallel partials reduced by row owners with the norm epilogues',
                 tokens=int(p['tokens']), ms_per_tree=round(ms, 3), tokens_per_s=round(p['tokens'] / (ms / 1000), 1),
@@ -858,7 +874,8 @@ def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):
                 max_abs_note='one GPU and the sharded model sum the row-parallel projections in different orders; '
                              'over 60 BF16 layers such differences reach the order of 1e-2 (the oracle against itself '
                              'with another GEMM summation order drifts as far)',
-                timing='CUDA events over the steps on every rank, max over ranks; tp_reduce from one traced tree')
+                timing='CUDA events over the steps on every rank, max over ranks; tp_reduce from one traced tree',
+                parity=parity)
 
 
 if __name__ == '__main__':

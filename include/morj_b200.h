@@ -80,7 +80,10 @@ int morj_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, v
  * 148-SM B200), 256-byte aligned, used by one stream only (launches on one stream run in order; two streams must
  * not share a workspace). morj_gemm_workspace_set zeroes the workspace's flags on `stream` and replaces any earlier
  * registration for (current device, stream); ptr = NULL removes it. morj_gemm_workspace_remove drops every
- * registration of `ptr` (call it before freeing the memory). At most 64 registrations. */
+ * registration of `ptr` (call it before freeing the memory). At most 64 registrations. The same workspace lets
+ * morj_gemm_bf16 run M <= 16 rows (plain and GeGLU epilogues; MORJ_GEMM_FORCE_* unset) on a weight-streaming kernel
+ * that cuts every tile's K range over all SMs and adds the pieces' FP32 partials in k order through the workspace
+ * (see morj_gemm_skinny_walk); without a workspace such calls take the tiled kernels. */
 int morj_gemm_workspace_bytes(unsigned long long* bytes);
 int morj_gemm_workspace_set(void* stream, void* ptr, unsigned long long bytes);
 int morj_gemm_workspace_remove(const void* ptr);

@@ -1,8 +1,9 @@
 """Tensor parallelism on every GPU of the box (2, 4 or 8 ranks), peer exchange and NCCL: a 2-layer model whose
 heads and intermediate size divide by 8 (hidden 512, 16 query / 8 KV heads of 64, GeGLU 2048) sharded over all
 ranks gives the label probabilities of the same model on one GPU (within 1e-2; two layers leave no depth for BF16
-roundings to accumulate), every rank the same ones. Child processes, one per GPU, NVLS off; skipped with fewer than
-two GPUs."""
+roundings to accumulate), every rank the same ones; on a 2,151-row request the engine cuts every exchange site in
+two and overlaps the parts, and gives the same bits as with the sites run whole. Child processes, one per GPU, NVLS
+off; skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -20,9 +21,11 @@ def config():
     return dict(text_config=cfg, image_token_id=4095, boi_token_id=4094, eoi_token_id=4093)
 
 
-def request():
+def request(prefix=150):
+    """4 branches over a shared prefix; with prefix 2000 a single step is long enough (2,151 rows) for the engine to
+    cut every exchange site in two and overlap them (`tp.overlap_split`, at 8 ranks too)."""
     rng = np.random.default_rng(3)
-    head = [int(v) for v in rng.integers(0, 4000, 150)]
+    head = [int(v) for v in rng.integers(0, 4000, prefix)]
     seqs = [head + [int(v) for v in rng.integers(0, 4000, n)] for n in (30, 45, 12, 64)]
     labels = [[7, 8, 9], [7, 8, 9], [10, 11], list(range(100, 140))]
     return seqs, labels
@@ -45,15 +48,22 @@ def _rank(rank, world, port, out):
         from morj_b200.checkpoint import random_state
         from morj_b200.lean_core import LeanGemma4
         top = config()
-        seqs, labels = request()
         res = {}
         for comm in ('peer', 'nccl'):
             model = LeanGemma4.from_state(top, random_state(top, seed=5), device=f'cuda:{rank}',
                                           tp_group=dist.group.WORLD, tp_comm=comm)
-            for steps in ((16384, 8192), (96, 64)):  # one step, and a pass cut into steps
-                model.single_max, model.step_tokens = steps
-                req = model.prepare(seqs, labels)
-                res[(comm, steps)] = np.concatenate(model.run(req, list(range(len(seqs)))))
+            for prefix in (150, 2000):
+                seqs, labels = request(prefix)
+                for steps in ((16384, 8192), (96, 64)):  # one step, and a pass cut into steps
+                    model.single_max, model.step_tokens = steps
+                    req = model.prepare(seqs, labels)
+                    res[(comm, prefix, steps)] = np.concatenate(model.run(req, list(range(len(seqs)))))
+            if comm == 'peer':  # the overlapped sites give the same bits as the sites run whole
+                model.tp_overlap = False
+                seqs, labels = request(2000)
+                whole = np.concatenate(model.run(model.prepare(seqs, labels), list(range(len(seqs)))))
+                model.tp_overlap = True
+                res['peer whole'] = whole
             if model.peer is not None:
                 dist.barrier()
                 model.peer.close()
@@ -74,11 +84,16 @@ def test_tensor_parallel_on_every_gpu_matches_one_gpu():
     from morj_b200.checkpoint import random_state
     from morj_b200.lean_core import LeanGemma4
     top = config()
-    seqs, labels = request()
     one = LeanGemma4.from_state(top, random_state(top, seed=5), device='cuda:0')
-    want = np.concatenate(one.run(one.prepare(seqs, labels), list(range(len(seqs)))))
-    for key, got in out[0].items():
-        err = np.abs(got - want).max()
+    want = {}
+    for prefix in (150, 2000):
+        seqs, labels = request(prefix)
+        want[prefix] = np.concatenate(one.run(one.prepare(seqs, labels), list(range(len(seqs)))))
+    res = dict(out[0])
+    whole = res.pop('peer whole')
+    assert np.array_equal(whole, res[('peer', 2000, (16384, 8192))])
+    for key, got in res.items():
+        err = np.abs(got - want[key[1]]).max()
         print(f'\n{world} ranks {key}: max |TP - one GPU| = {err:.2e}')
         assert err <= 1e-2, (world, key, err)
         for r in range(1, world):

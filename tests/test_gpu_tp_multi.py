@@ -58,8 +58,9 @@ def _rank(rank, world, port, out):
                     model.single_max, model.step_tokens = steps
                     req = model.prepare(seqs, labels)
                     res[(comm, prefix, steps)] = np.concatenate(model.run(req, list(range(len(seqs)))))
-            if comm == 'peer':  # the same request with every site run whole
+            if comm == 'peer':  # the same one-step request with every site run whole
                 model.tp_overlap = False
+                model.single_max, model.step_tokens = 16384, 8192
                 seqs, labels = request(2000)
                 whole = np.concatenate(model.run(model.prepare(seqs, labels), list(range(len(seqs)))))
                 model.tp_overlap = True

@@ -487,9 +487,6 @@ def main():
                                          'attention-text-sliding', 'attention-text-global', 'peer-reduce',
                                          'attn-epilogue', 'mlp-epilogue', 'vision'],
                     help='time one kernel alone instead of the tree forward')
-    ap.add_argument('--no-tp-overlap', action='store_true',
-                    help='tensor parallelism over peer memory: run every exchange site whole (no overlap of the first '
-                         'rows\' reduction with the GEMM of the rest)')
     ap.add_argument('--no-split', action='store_true',
                     help='no split-tile workspace registered (every GEMM tile computed whole)')
     ap.add_argument('--force', type=lambda v: int(v, 0), default=0,
@@ -539,7 +536,6 @@ def main():
     t_init = time.perf_counter()
     model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD if tp else None,
                                    tp_comm=args.tp_comm)
-    model.tp_overlap = not args.no_tp_overlap
     if args.no_split and model.gemm_ws is not None:  # every GEMM tile computed whole
         model.gemm_ws.close()
         model.gemm_ws = None
@@ -827,7 +823,6 @@ def tp_leg(args, one_gpu, top, dev, world, rank, barrier, max_over_ranks):
     barrier()
     t_init = time.perf_counter()
     model = LeanGemma4.random_init(top, seed=0, device=dev, tp_group=dist.group.WORLD, tp_comm='peer')
-    model.tp_overlap = not args.no_tp_overlap
     barrier()
     init_s = time.perf_counter() - t_init
     with torch.inference_mode():

@@ -199,7 +199,6 @@ class LeanGemma4:
             raise ValueError(f"tp_comm must be 'peer' or 'nccl', not {tp_comm!r}")
         self.tp_group, self.tp_world, self.tp_rank = tp_group, 1, 0
         self.peer = None
-        self.tp_overlap, self._side = True, None  # see _peer_site
         if tp_group is not None:
             import torch.distributed as dist
             from .tp import shard_config, shard_getter
@@ -615,48 +614,17 @@ class LeanGemma4:
         """Tensor parallelism over peer memory: the row-parallel projection a . w^T delivers its partial tiles to the
         row blocks' owners, each owner reduces its rows with the post-attention (mode 0) or post-MLP (mode 1)
         epilogue and pushes the new h rows (x rows too when `push_x`) to every rank, then the stream waits for all
-        of h (`morj_gemm_bf16_peer`, `morj_peer_reduce`, `morj_peer_wait`).
-
-        With `tp_overlap` (default) and enough rows, the site is cut at `tp.overlap_split`: the GEMM of the first
-        rows, then the reduction of those rows on a side stream while the GEMM of the rest runs on this one, then the
-        rest's reduction here. The two reductions touch disjoint rows and counters; the side one waits only on the
-        peers' first-part tiles (its own finished before it starts), so no kernel waits on a kernel running beside it
-        on this GPU. Each part is addressed by a descriptor shifted to its first row (`tp.shifted_desc`)."""
+        of h (`morj_gemm_bf16_peer`, `morj_peer_reduce`, `morj_peer_wait`)."""
         import ctypes
-        from .tp import overlap_split, partial_target, row_target, shifted_desc
+        from .tp import partial_target, row_target
         ex, s = self.peer, self._stream()
         desc = ctypes.addressof(ex.desc)
         K, N = a.shape[1], w.shape[0]
+        self._k('gemm', 'morj_gemm_bf16_peer', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), n, N, K, desc,
+                s, flops=2 * n * N * K)
         ex.sites += 1
-        pt = partial_target(ex.sites, ex.world, self.hidden)
-        cut = overlap_split(n, ex.world) if self.tp_overlap else 0
-        if cut:
-            lo = shifted_desc(ex.desc, 0, max_blocks=cut // 128)  # no padding: the blocks past `cut` are real
-            hi = shifted_desc(ex.desc, cut)
-            if self._side is None:
-                self._side = torch.cuda.Stream(device=self.device)
-            main = torch.cuda.current_stream(self.device)
-            self._k('gemm', 'morj_gemm_bf16_peer', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), cut, N, K,
-                    desc, s, flops=2 * cut * N * K)
-            first_done = torch.cuda.Event()
-            first_done.record(main)
-            self._side.wait_event(first_done)
-            with torch.cuda.stream(self._side):
-                self._k('tp_reduce', 'morj_peer_reduce', ctypes.addressof(lo), mode, cut, w_a.data_ptr(),
-                        _ptr(scalar), _ptr(w_b), self.eps, has_next, push_x, pt, self._side.cuda_stream)
-            reduced = torch.cuda.Event()
-            reduced.record(self._side)
-            a_hi = a.data_ptr() + cut * a.stride(0) * a.element_size()
-            self._k('gemm', 'morj_gemm_bf16_peer', a_hi, a.stride(0), w.data_ptr(), w.stride(0), n - cut, N, K,
-                    ctypes.addressof(hi), s, flops=2 * (n - cut) * N * K)
-            self._k('tp_reduce', 'morj_peer_reduce', ctypes.addressof(hi), mode, n - cut, w_a.data_ptr(),
-                    _ptr(scalar), _ptr(w_b), self.eps, has_next, push_x, pt, s)
-            main.wait_event(reduced)
-        else:
-            self._k('gemm', 'morj_gemm_bf16_peer', a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), n, N, K,
-                    desc, s, flops=2 * n * N * K)
-            self._k('tp_reduce', 'morj_peer_reduce', desc, mode, n, w_a.data_ptr(), _ptr(scalar), _ptr(w_b),
-                    self.eps, has_next, push_x, pt, s)
+        self._k('tp_reduce', 'morj_peer_reduce', desc, mode, n, w_a.data_ptr(), _ptr(scalar), _ptr(w_b), self.eps,
+                has_next, push_x, partial_target(ex.sites, ex.world, self.hidden), s)
         self._k('tp_reduce', 'morj_peer_wait', desc, n, row_target(ex.sites), s)
 
     def _peer_rows(self, n):

@@ -93,34 +93,6 @@ def owner(block, world):
     return block % world
 
 
-def overlap_split(n, world):
-    """Where a site's rows are cut so the first part's reduction can run beside the row-parallel GEMM of the rest:
-    half of `n`, rounded down to whole groups of `world` row blocks (so block b keeps its owner b % world in the
-    shifted part); 0 = no cut (too few rows)."""
-    unit = BLOCK * world
-    return (n // 2) // unit * unit
-
-
-def shifted_desc(desc, row0, max_blocks=None):
-    """A copy of `desc` (a `morj_peer_t`) that starts at row `row0` of every buffer (row0 a multiple of 128 x world,
-    so the owners of the shifted blocks are unchanged), holding `max_blocks` blocks (default: the rest)."""
-    from . import _native as nat
-    b0 = row0 // BLOCK
-    if row0 % (BLOCK * desc.world) or b0 > desc.max_blocks:
-        raise ValueError(f'row {row0} does not start a group of {desc.world} row blocks inside the exchange')
-    d = nat.PeerDesc()
-    d.world, d.rank, d.hidden = desc.world, desc.rank, desc.hidden
-    d.max_blocks = desc.max_blocks - b0 if max_blocks is None else max_blocks
-    row_bytes = desc.hidden * 2
-    for r in range(desc.world):
-        d.part[r] = desc.part[r] + row0 * row_bytes
-        d.x[r] = desc.x[r] + row0 * row_bytes
-        d.h[r] = desc.h[r] + row0 * row_bytes
-        d.partials[r] = desc.partials[r] + b0 * 8
-        d.rows[r] = desc.rows[r] + b0 * 8
-    return d
-
-
 def partial_target(sites, world, hidden):
     """A block's partial-column counter after `sites` reductions: every rank delivers 4 x hidden columns per block
     per site (4 epilogue warps of 32 rows, each counting the columns of every tile it stored)."""

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from morj_b200 import _native as nat
-from morj_b200.tp import BLOCK, exchange_layout, overlap_split, owner, partial_target, row_target, shifted_desc
+from morj_b200.tp import BLOCK, exchange_layout, owner, partial_target, row_target
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device('cuda', 0)
@@ -45,25 +45,16 @@ class Group:
         """Every rank's partial rows [0, n): [world, n, hidden], read from their part buffers."""
         return torch.stack([self.region(r, 'part', n) for r in range(self.world)])
 
-    def site(self, a, w, mode, n, w_a, scalar, w_b, has_next, push_x, cut=0):
-        """One site; with `cut` > 0 in two parts as the engine overlaps them (rows [0, cut) with descriptors that hold
-        only those blocks, then rows [cut, n) with descriptors shifted to row `cut`), here one after the other."""
+    def site(self, a, w, mode, n, w_a, scalar, w_b, has_next, push_x):
         s = stream()
+        for r in range(self.world):
+            nat.call('morj_gemm_bf16_peer', a[r].data_ptr(), a[r].stride(0), w[r].data_ptr(), w[r].stride(0), n,
+                     self.hidden, a[r].shape[1], ctypes.addressof(self.descs[r]), s)
         self.sites += 1
-        target = partial_target(self.sites, self.world, self.hidden)
-        sc = scalar.data_ptr() if scalar is not None else None
-        parts = [(0, n, self.descs, self.descs)]  # (first row, rows, GEMM descriptors, reduce descriptors)
-        if cut:
-            lo = [shifted_desc(d, 0, max_blocks=cut // BLOCK) for d in self.descs]
-            hi = [shifted_desc(d, cut) for d in self.descs]
-            parts = [(0, cut, self.descs, lo), (cut, n - cut, hi, hi)]
-        for r0, rows, gemm_descs, reduce_descs in parts:
-            for r in range(self.world):
-                nat.call('morj_gemm_bf16_peer', a[r][r0:].data_ptr(), a[r].stride(0), w[r].data_ptr(),
-                         w[r].stride(0), rows, self.hidden, a[r].shape[1], ctypes.addressof(gemm_descs[r]), s)
-            for r in range(self.world):
-                nat.call('morj_peer_reduce', ctypes.addressof(reduce_descs[r]), mode, rows, w_a.data_ptr(), sc,
-                         w_b.data_ptr(), 1e-6, has_next, push_x, target, s)
+        for r in range(self.world):
+            nat.call('morj_peer_reduce', ctypes.addressof(self.descs[r]), mode, n, w_a.data_ptr(),
+                     scalar.data_ptr() if scalar is not None else None, w_b.data_ptr(), 1e-6, has_next, push_x,
+                     partial_target(self.sites, self.world, self.hidden), s)
         for r in range(self.world):
             nat.call('morj_peer_wait', ctypes.addressof(self.descs[r]), n, row_target(self.sites), s)
 
@@ -72,10 +63,9 @@ def norm_weight(g, hidden):
     return (1 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).to(torch.bfloat16)
 
 
-@pytest.mark.parametrize('cut', [False, True])  # sites in two parts where the engine cuts them (tp.overlap_split)
 @pytest.mark.parametrize('world', [1, 2, 3, 4, 6, 8])  # the reduce kernel's rank bound W = 2, 4, 8
-def test_peer_sites_match_the_replicated_epilogues(world, cut):
-    hidden, max_rows, k = 256, 2200, 96
+def test_peer_sites_match_the_replicated_epilogues(world):
+    hidden, max_rows, k = 256, 1100, 96
     g = torch.Generator(device=DEV).manual_seed(world)
     grp = Group(world, hidden, max_rows)
     x0 = torch.randn(max_rows, hidden, device=DEV, generator=g).to(torch.bfloat16)
@@ -87,15 +77,12 @@ def test_peer_sites_match_the_replicated_epilogues(world, cut):
     scalar = torch.tensor([0.75], device=DEV).to(torch.bfloat16)
     # (mode, rows, has_next, push_x): row counts change between sites, so blocks are padded and then used
     sites = [(0, 300, 1, 0), (1, 300, 1, 0), (0, 1100, 1, 0), (1, 1100, 1, 1), (0, 129, 1, 0), (1, 129, 0, 1),
-             (0, 2200, 1, 0), (1, 2200, 1, 1), (0, 1, 1, 0), (1, 1000, 1, 0)]
-    cuts = 0
+             (0, 1, 1, 0), (1, 1000, 1, 0)]
     for mode, n, has_next, push_x in sites:
         a = [torch.randn(n, k, device=DEV, generator=g).to(torch.bfloat16) for _ in range(world)]
         w = [(torch.randn(hidden, k, device=DEV, generator=g) * 0.1).to(torch.bfloat16) for _ in range(world)]
-        c = overlap_split(n, world) if cut else 0
-        cuts += c > 0
         grp.site(a, w, mode, n, w_post, scalar if mode == 1 else None, w_pre if mode == 0 else w_next, has_next,
-                 push_x, c)
+                 push_x)
         torch.cuda.synchronize()
         assert nat.device_error(stream()) == 0
         parts = grp.delivered(n)
@@ -120,7 +107,6 @@ def test_peer_sites_match_the_replicated_epilogues(world, cut):
             assert torch.equal(xr[rows], x_ref[rows]), (mode, n, r)
             if mode == 0 or has_next:
                 assert torch.equal(grp.region(r, 'h', max_rows)[:n], h_ref[:n]), (mode, n, r)
-    assert cuts >= 2 or not cut  # (the two 2200-row sites are cut at every world size)
 
 
 def test_peer_waits_run_out_and_report():
